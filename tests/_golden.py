@@ -1,0 +1,34 @@
+"""Helpers for loading the committed golden fixtures (tests/golden)."""
+import json
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+QUANT_FUNCS = [
+    ("nvfp4_naive", 0, 0), ("nvfp4_optimal", 0, 1),
+    ("mxfp4_naive", 1, 0), ("mxfp4_optimal", 1, 1),
+    ("mxfp4_naive_torch", 1, 3), ("mxfp4_optimal_torch", 1, 4),
+]
+
+
+def load(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def digests():
+    with open(os.path.join(GOLDEN, "digests.json")) as f:
+        return json.load(f)
+
+
+def same_bits(a, b):
+    a = np.ascontiguousarray(a, np.float32).reshape(-1).view(np.uint32)
+    b = np.ascontiguousarray(b, np.float32).reshape(-1).view(np.uint32)
+    return a.shape == b.shape and bool((a == b).all())
+
+
+def n_diff_bits(a, b):
+    a = np.ascontiguousarray(a, np.float32).reshape(-1).view(np.uint32)
+    b = np.ascontiguousarray(b, np.float32).reshape(-1).view(np.uint32)
+    return int((a != b).sum())
