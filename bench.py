@@ -1,0 +1,330 @@
+"""Benchmark: G weights/s quantized (NVFP4/MXFP4 naive + SSE-optimal), config 1.
+
+One step = the eight quantizations of configuration 1 -- NVFP4 and MXFP4, block
+16 and 32, naive and SSE-optimal -- each over a full 2560x9728 bf16 weight
+(the Qwen3-4B down_proj shape; seeded synthetic N(0, 0.02^2) with 0.1% x20
+outliers), writing native outputs (scale bytes, packed E2M1 nibbles, bf16
+dequant).  The eight calls of a step read eight different weights from a pool
+of eight (400 MB > the 126 MB L2), so every call streams its input from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): weak scaling, every rank quantizes its
+own pool (rank-seeded); no collective on the data path; time = max over ranks.
+--impl reference times the reference algorithm's CPU implementation (the
+oracle restatement, all host threads) on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, K = 2560, 9728
+WEIGHTS = M * K
+CALLS = [(fmt, bs, meth) for fmt in (0, 1) for bs in (16, 32) for meth in (0, 1)]  # 8 per step
+FMT_NAME = {0: "nvfp4", 1: "mxfp4"}
+METH_NAME = {0: "naive", 1: "optimal"}
+POOL = 8
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[5:9]) if "Active" in v and "Not" not in v})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def make_pool(rank, device):
+    from qwantize_b200.synthetic import make_weight
+    return [make_weight(M, K, seed=1000 * rank + i).to(device) for i in range(POOL)]
+
+
+def alloc_outputs(device):
+    out = {}
+    for bs in (16, 32):
+        nb = WEIGHTS // bs
+        out[bs] = (torch.empty(nb, dtype=torch.uint8, device=device),
+                   torch.empty(nb * bs // 2, dtype=torch.uint8, device=device),
+                   torch.empty(WEIGHTS, dtype=torch.bfloat16, device=device))
+    return out
+
+
+def run_step(L, pool, outs, step, stream):
+    """Eight C-ABI launches, one per call of the step (inputs resident in HBM)."""
+    for k, (fmt, bs, meth) in enumerate(CALLS):
+        x = pool[(step * len(CALLS) + k) % POOL]
+        codes, packed, dqb = outs[bs]
+        st = L.lib.qz_quantize(x.data_ptr(), 1, WEIGHTS // bs, bs, fmt, meth, None, 0, None, None,
+                               None, codes.data_ptr(), packed.data_ptr(), dqb.data_ptr(), stream)
+        if st:
+            raise RuntimeError(L.lib.qz_last_error().decode())
+
+
+class _Lib:
+    def __init__(self):
+        from qwantize_b200 import _lib
+        self.lib = _lib.load()
+
+
+def cpu_oracle_workload(threads):
+    """The reference algorithm on the host (oracle restatement): the full
+    config-1 workload once.  Returns (seconds, weights, n_candidates)."""
+    from oracle import oracle
+    from qwantize_b200.synthetic import make_weight
+    W = make_weight(M, K, seed=0).view(torch.int16).numpy().view(np.uint16)
+    t0 = time.perf_counter()
+    ncand = {}
+    for fmt, bs, meth in CALLS:
+        _, _, _, nc = oracle.quantize(W, bs, fmt, meth, threads=threads)
+        ncand[(fmt, bs, meth)] = nc
+    return time.perf_counter() - t0, WEIGHTS * len(CALLS), ncand
+
+
+def bench_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cpu_oracle_workload(threads)  # warm-up of the library / page cache
+    for _ in range(max(0, args.warmup - 1)):
+        cpu_oracle_workload(threads)
+    t, n = 0.0, 0
+    for _ in range(args.steps):
+        dt, w, _ = cpu_oracle_workload(threads)
+        t += dt
+        n += w
+    v = n / t / 1e9
+    line = {"impl": "reference", "metric": "G weights/s quantized (NVFP4/MXFP4 naive+SSE, config 1)",
+            "value": v, "unit": "G weights/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config1: nvfp4+mxfp4 x bs16+bs32 x naive+optimal on one 2560x9728 bf16 weight",
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": v, "unit": "G weights/s", "cores": threads, "kind": "port",
+                             "sample": "the full config-1 workload (8 quantizations of 24.9M weights) per step"},
+            "e2e": {"value": v, "unit": "G weights/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def bench_ours(args):
+    ws, rank, local = dist_env()
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    L = _Lib()
+    pool = make_pool(rank, device)
+    outs = alloc_outputs(device)
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    for w in range(args.warmup):
+        run_step(L, pool, outs, w, sp)
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for s in range(args.steps):
+            run_step(L, pool, outs, s, sp)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    total_weights = WEIGHTS * len(CALLS) * args.steps * ws
+    value = total_weights / (ms / 1e3) / 1e9
+
+    # ---- dominant kernel alone: NVFP4 bs16 SSE-optimal, CUDA events ----
+    reps = 20
+    per = {}
+    for fmt, bs, meth in CALLS:
+        codes, packed, dqb = outs[bs]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(stream)
+        for r in range(reps):
+            x = pool[r % POOL]
+            L.lib.qz_quantize(x.data_ptr(), 1, WEIGHTS // bs, bs, fmt, meth, None, 0, None, None, None,
+                              codes.data_ptr(), packed.data_ptr(), dqb.data_ptr(), sp)
+        ev[1].record(stream)
+        torch.cuda.synchronize(device)
+        per[(fmt, bs, meth)] = ev[0].elapsed_time(ev[1]) / reps
+    dom = max(per, key=per.get)
+    fmt, bs, meth = dom
+    bytes_per_w = 2 + 0.5 + 1.0 / bs + 2  # bf16 in; nibbles + scale byte + bf16 dequant out
+    achieved = WEIGHTS * bytes_per_w / (per[dom] / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # ---- end to end through the public API, host (pinned) buffers ----
+    import qwantize_b200 as q
+    host_pool = [p.cpu().pin_memory() for p in pool[:2]]
+    h2d = d2h = 0
+    torch.cuda.synchronize(device)
+    barrier()
+    t0 = time.perf_counter()
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ee0.record(stream)
+    e2e_steps = max(1, min(args.steps, 3))
+    for s in range(e2e_steps):
+        for k, (f, b, m) in enumerate(CALLS):
+            Wh = host_pool[k % 2]
+            Wd = Wh.to(device, non_blocking=True).reshape(M, K // b, b)
+            fn = q.nvfp4_quantize_packed if f == 0 else q.mxfp4_quantize_packed
+            codes, packed, dqb = fn(Wd, method=METH_NAME[m], return_dequant=True)
+            res = [t.to("cpu", non_blocking=True) for t in (codes, packed, dqb)]
+            if s == 0:
+                h2d += Wh.numel() * 2
+                d2h += sum(t.numel() * t.element_size() for t in (codes, packed, dqb))
+    ee1.record(stream)
+    torch.cuda.synchronize(device)
+    del res
+    e2e_ms = ee0.elapsed_time(ee1)
+    if ws > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = WEIGHTS * len(CALLS) * e2e_steps * ws / (e2e_ms / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        dt, w, ncand = cpu_oracle_workload(threads)
+        cpu = {"value": w / dt / 1e9, "unit": "G weights/s", "cores": threads, "kind": "port",
+               "sample": "the full config-1 workload once (8 quantizations of 24.9M weights)",
+               "seconds": dt}
+        nc = ncand.get(dom, 0) / (WEIGHTS // bs)
+    else:
+        nc = None
+
+    if rank == 0:
+        issue = None
+        if meth == 1 and nc is not None:
+            # lane-op cost model fixed before building: 12 per element for the
+            # bounds, 10 per element per full SSE evaluation (baseline + each
+            # candidate), 4 per element per clip check
+            ops_per_w = 12 + 10 * (1 + nc) + 4 * nc
+            clk = clk.summary()
+            mhz = clk.get("sm_mhz") or 1965.0
+            peak_ops = 148 * 128 * mhz * 1e6
+            ach_ops = WEIGHTS * ops_per_w / (per[dom] / 1e3)
+            issue = {"unit": "lane-op/s", "achieved": ach_ops, "peak": peak_ops, "frac": ach_ops / peak_ops,
+                     "candidates_per_block": nc, "lane_ops_per_weight": ops_per_w,
+                     "peak_basis": "148 SMs x 128 FP32 lanes x median SM clock"}
+        else:
+            clk = clk.summary()
+        line = {
+            "metric": "G weights/s quantized (NVFP4/MXFP4 naive+SSE, config 1)",
+            "value": value, "unit": "G weights/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config1: nvfp4+mxfp4 x bs16+bs32 x naive+optimal, 2560x9728 bf16 weight per call, native outputs",
+                       "weights_per_step_per_gpu": WEIGHTS * len(CALLS), "parallelism": f"independent x{ws}",
+                       "l2": "each call reads a different weight of an 8-weight pool (400 MB > L2)"},
+            "gpu_launches": len(CALLS) * args.steps,
+            "per_kernel_ms": {f"{FMT_NAME[f]}_{METH_NAME[m]}_bs{b}": v for (f, b, m), v in per.items()},
+            "roofline": {"kernel": f"quantize {FMT_NAME[fmt]} {METH_NAME[meth]} bs{bs}", "bound": "hbm",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "bytes_per_weight": bytes_per_w, "issue": issue},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "G weights/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        bench_reference(args)
+    else:
+        bench_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+/*
+ * qwantize_b200.h -- C ABI of the B200 (sm_100a) block-scale quantization
+ * library libqwantize_b200.so.
+ *
+ * The reference (qwantize v0.1.2) is a pure-Python package with no FFI; each
+ * entry point below replaces the functions of its Python API named beside it
+ * (paths relative to the qwantize project root).  The Python package
+ * qwantize_b200 binds them with ctypes and keeps the reference's function
+ * names, keyword arguments, returned tuples and AssertionError behaviour.
+ *
+ * Conventions
+ *   - Pointers are device pointers unless stated otherwise.  Inputs are never
+ *     modified.  A NULL output pointer means "do not write it".
+ *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) and returns a status code; qz_last_error() returns a
+ *     message for the last non-zero status of the calling thread.
+ *   - Blocked layout: `n_blocks` contiguous blocks of `block_size` (16 or 32)
+ *     elements, i.e. the reference's W.movedim(dim, -1).reshape(-1, bs).
+ *   - Naive and SSE results are bit-identical to the reference's pure-PyTorch
+ *     CPU path for bf16 and fp16 inputs (signed zeros and NaN bit patterns
+ *     included).
+ */
+#ifndef QWANTIZE_B200_H
+#define QWANTIZE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QZ_API __attribute__((visibility("default")))
+#else
+#define QZ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define QZ_OK 0
+#define QZ_ERR_INVALID 1     /* bad argument (Python raises AssertionError / ValueError) */
+#define QZ_ERR_CUDA 2        /* CUDA runtime / driver error */
+#define QZ_ERR_TIMEOUT 3     /* a bounded device-side wait gave up */
+#define QZ_ERR_UNSUPPORTED 4 /* device is not sm_100 */
+
+/* element types */
+#define QZ_DTYPE_F32 0
+#define QZ_DTYPE_BF16 1
+#define QZ_DTYPE_F16 2
+
+/* formats */
+#define QZ_FMT_NVFP4 0 /* E2M1 codes, FP8-E4M3 scale per block (126 positive values) */
+#define QZ_FMT_MXFP4 1 /* E2M1 codes, UE8M0 power-of-two scale per block (254 values) */
+
+/* scale-selection methods */
+#define QZ_METHOD_NAIVE 0        /* nvfp4/reference.py:89-126, mxfp4/reference.py:89-129 */
+#define QZ_METHOD_SSE 1          /* nvfp4/reference.py:129-239, mxfp4/reference.py:132-238 */
+#define QZ_METHOD_HESSIAN 2      /* nvfp4/reference.py:266-407, mxfp4/reference.py:241-374 */
+#define QZ_METHOD_NAIVE_ARGMIN 3 /* mxfp4/kernels.py:267-314 mxfp4_naive_torch */
+#define QZ_METHOD_TWO_ARGMIN 4   /* mxfp4/kernels.py:317-377 mxfp4_optimal_torch */
+
+/* Gram modes */
+#define QZ_GRAM_FULL 0      /* H = X^T X, (K, K) fp32, symmetric */
+#define QZ_GRAM_BLOCKDIAG 1 /* H_j = X_j^T X_j, (K/bs, bs, bs) fp32 */
+
+/*
+ * qz_quantize -- per-block scale selection + E2M1 quantization in one pass.
+ * Replaces nvfp4_naive / nvfp4_optimal / nvfp4_optimal_hessian and the
+ * *_triton variants (nvfp4/reference.py:89-407, nvfp4/kernels.py:248-427),
+ * mxfp4_naive / mxfp4_optimal / mxfp4_optimal_hessian / *_triton / *_torch
+ * (mxfp4/reference.py:89-374, mxfp4/kernels.py:164-377).
+ *   x           n_blocks*block_size elements of x_dtype, 16-byte aligned
+ *   h_blocks    (n_col_blocks, bs, bs) fp32 block Hessians for
+ *               QZ_METHOD_HESSIAN (block b uses h_blocks[b % n_col_blocks])
+ *   scales      (n_blocks) fp32 chosen scales (the reference's `scales`)
+ *   quants      (n_blocks*bs) fp32 signed codebook values (`quants`)
+ *   dq          (n_blocks*bs) fp32 quants*scales (the dequant)
+ *   scale_codes (n_blocks) E4M3 byte (NVFP4) or UE8M0 biased exponent (MXFP4)
+ *   packed      (n_blocks*bs/2) E2M1 nibbles; element 2i in the low nibble of
+ *               byte i, bit 3 = sign (the layout fp4.py:117-282 decodes)
+ *   dq_bf16     (n_blocks*bs) bf16 dequant (exact: dequant values fit bf16)
+ */
+QZ_API int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, int format,
+                int method, const float* h_blocks, int64_t n_col_blocks, float* scales,
+                float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,
+                uint16_t* dq_bf16, void* stream);
+
+/*
+ * qz_dequantize -- out = quants * scales per block.  Replaces nvfp4_dequantize
+ * (nvfp4/reference.py:537-549) and mxfp4_dequantize (mxfp4/reference.py:377-389)
+ * in the blocked layout.
+ */
+QZ_API int qz_dequantize(const float* scales, const float* quants, int64_t n_blocks, int block_size,
+                  float* out, void* stream);
+
+/*
+ * qz_dequantize_packed -- packed E2M1 nibbles + scale bytes -> fp32 and/or
+ * bf16.  Native-storage counterpart of qz_dequantize (the reference keeps fp32
+ * only; its byte scales are s.to(float8_e4m3fn) in
+ * bench/nvfp4_scale_distance.py:20-22 and scales_to_ue8m0_exponent in
+ * mxfp4/reference.py:392-403).
+ */
+QZ_API int qz_dequantize_packed(const uint8_t* packed, const uint8_t* scale_codes, int64_t n_blocks,
+                         int block_size, int format, float* out_f32, uint16_t* out_bf16,
+                         void* stream);
+
+/*
+ * qz_fp4_unpack -- packed nibbles -> int8 values of the doubled codebook
+ * {0,1,2,3,4,6,8,12} with sign.  Replaces fp4_unpack (fp4.py:257-282);
+ * n_bytes must be a multiple of 4 (fp4.py:273).
+ */
+QZ_API int qz_fp4_unpack(const uint8_t* packed, int64_t n_bytes, int8_t* out, void* stream);
+
+/*
+ * qz_gram -- H = X^T X in fp32 from bf16 X (T, K) row-major, on the tcgen05
+ * tensor cores.  Replaces the block-Hessian build of nvfp4/reference.py:304-317
+ * (also nvfp4/kernels.py:386-397, mxfp4/reference.py:271-284).
+ * QZ_GRAM_FULL writes the symmetric (K, K) matrix; QZ_GRAM_BLOCKDIAG writes
+ * (K/bs, bs, bs).  accumulate != 0 adds into H instead of overwriting it.
+ */
+QZ_API int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int block_size, int accumulate,
+            float* H, void* stream);
+
+/*
+ * qz_weight_error_sums -- sums[0] += sum (W_dq - W)^2, sums[1] += sum W^2 in
+ * double (metrics.py:23-27).  W and W_dq are n elements of w_dtype / dq_dtype.
+ */
+QZ_API int qz_weight_error_sums(const void* W, int w_dtype, const void* W_dq, int dq_dtype, int64_t n,
+                         double* sums, void* stream);
+
+/*
+ * qz_output_error_sums -- sums[0] += sum ((X W_dq^T) - (X W^T))^2 and
+ * sums[1] += sum (X W^T)^2 (metrics.py:29-50), one tcgen05 GEMM pass over
+ * bf16 X (T, K) against bf16 W and W_dq (M, K) with the reduction fused into
+ * the epilogue (the T x M products are never written).
+ */
+QZ_API int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, const uint16_t* W,
+                         const uint16_t* W_dq, int64_t M, double* sums, void* stream);
+
+/* Host helpers. */
+QZ_API int qz_scale_table(int format, float* out_host, int* n_out); /* 126 / 254 ascending values */
+QZ_API const char* qz_last_error(void);
+QZ_API int qz_version(void);
+QZ_API int qz_device_ok(void); /* QZ_OK if the current device is sm_100 */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWANTIZE_B200_H */

@@ -1,0 +1,119 @@
+"""Host side of the drop-in API: layout plumbing around the C ABI.
+
+Mirrors the reference's wrappers (qwantize v0.1.2, e.g. nvfp4/reference.py:106-126):
+``dim`` is moved last and the tensor viewed as (N, bs) blocks; outputs are
+reshaped back to the reference's shapes.  All arithmetic runs in the sm_100a
+kernels; a CPU tensor is copied to the current CUDA device and the results
+are copied back (there is no CPU implementation).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+
+def cuda_device(t: torch.Tensor) -> torch.device:
+    if t.is_cuda:
+        return t.device
+    if not torch.cuda.is_available():
+        raise RuntimeError("qwantize_b200 needs a CUDA (sm_100a) device; none is available")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _blocks(W: torch.Tensor, dim: int):
+    dim = dim % W.ndim
+    block_size = W.shape[dim]
+    assert block_size in (16, 32)
+    dev = cuda_device(W)
+    x = W.movedim(dim, -1)
+    batch_shape = x.shape[:-1]
+    if x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        x = x.float()  # W.float() in the reference: float64 etc. round once to fp32
+    x = x.to(dev, non_blocking=True).reshape(-1, block_size)
+    if not x.is_contiguous():
+        x = x.contiguous()
+    if x.data_ptr() % 16:  # a view at an odd offset: the kernels load 16-byte vectors
+        x = x.clone()
+    return dim, block_size, batch_shape, x, dev
+
+
+def quantize_fp32(W, dim, return_dequant, fmt, method, H_blocks=None):
+    """Reference-shaped result: fp32 (scales, quants[, dq])."""
+    dim, bs, batch_shape, x, dev = _blocks(W, dim)
+    N = x.shape[0]
+    scales = torch.empty(N, dtype=torch.float32, device=dev)
+    quants = torch.empty(N, bs, dtype=torch.float32, device=dev)
+    dq = torch.empty(N, bs, dtype=torch.float32, device=dev) if return_dequant else None
+    J = 0
+    if method == L.METHOD_HESSIAN:
+        J = H_blocks.shape[0]
+        M_dim = N // J if J else 0
+        assert N == M_dim * J
+    st = L.load().qz_quantize(
+        L.ptr(x), L.dtype_code(x.dtype), N, bs, fmt, method, L.ptr(H_blocks), J,
+        L.ptr(scales), L.ptr(quants), L.ptr(dq), None, None, None, L.stream_ptr(dev))
+    L.check(st, "qz_quantize")
+    out_dev = W.device
+    res = (scales.reshape(*batch_shape).to(out_dev),
+           quants.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev))
+    if return_dequant:
+        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev),)
+    return res
+
+
+def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None):
+    """Native storage: (scale_codes uint8, packed uint8 (..., bs/2)[, dq bf16]).
+
+    scale_codes are E4M3 bytes (NVFP4) or UE8M0 biased exponents (MXFP4);
+    packed holds two E2M1 nibbles per byte, element 2i in the low nibble."""
+    dim, bs, batch_shape, x, dev = _blocks(W, dim)
+    N = x.shape[0]
+    codes = torch.empty(N, dtype=torch.uint8, device=dev)
+    packed = torch.empty(N, bs // 2, dtype=torch.uint8, device=dev)
+    dq = torch.empty(N, bs, dtype=torch.bfloat16, device=dev) if return_dequant else None
+    J = 0
+    if method == L.METHOD_HESSIAN:
+        J = H_blocks.shape[0]
+        assert N % J == 0
+    st = L.load().qz_quantize(
+        L.ptr(x), L.dtype_code(x.dtype), N, bs, fmt, method, L.ptr(H_blocks), J,
+        None, None, None, L.ptr(codes), L.ptr(packed), L.ptr(dq), L.stream_ptr(dev))
+    L.check(st, "qz_quantize")
+    res = (codes.reshape(*batch_shape), packed.reshape(*batch_shape, bs // 2))
+    if return_dequant:
+        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim),)
+    return res
+
+
+def dequantize(scales, quants, dim=-1):
+    """quants * scales.unsqueeze(dim) (nvfp4/reference.py:537-549)."""
+    dim = dim % quants.ndim
+    bs = quants.shape[dim]
+    assert bs in (16, 32)
+    dev = cuda_device(quants)
+    q = quants.movedim(dim, -1).to(dev, torch.float32).contiguous()
+    batch_shape = q.shape[:-1]
+    s = scales.to(dev, torch.float32).reshape(-1).contiguous()
+    assert s.numel() * bs == q.numel()
+    out = torch.empty_like(q)
+    L.check(L.load().qz_dequantize(L.ptr(s), L.ptr(q), s.numel(), bs, L.ptr(out),
+                                   L.stream_ptr(dev)), "qz_dequantize")
+    return out.reshape(*batch_shape, bs).movedim(-1, dim).to(quants.device)
+
+
+def dequantize_native(scale_codes, packed, fmt, dtype=torch.bfloat16):
+    """(scale_codes (...), packed (..., bs/2)) -> dequantized (..., bs)."""
+    dev = cuda_device(packed)
+    bs = packed.shape[-1] * 2
+    assert bs in (16, 32)
+    p = packed.to(dev).contiguous()
+    c = scale_codes.to(dev).contiguous()
+    n_blocks = c.numel()
+    out = torch.empty(*packed.shape[:-1], bs, dtype=dtype, device=dev)
+    f32 = out if dtype == torch.float32 else None
+    b16 = out if dtype == torch.bfloat16 else None
+    assert f32 is not None or b16 is not None, "dtype must be float32 or bfloat16"
+    L.check(L.load().qz_dequantize_packed(L.ptr(p), L.ptr(c), n_blocks, bs, fmt, L.ptr(f32),
+                                          L.ptr(b16), L.stream_ptr(dev)), "qz_dequantize_packed")
+    return out.to(packed.device)

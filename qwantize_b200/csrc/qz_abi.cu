@@ -1,0 +1,186 @@
+// qz_abi.cu -- the extern "C" entry points declared in include/qwantize_b200.h:
+// argument validation, status codes, per-thread error messages, dispatch.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/qwantize_b200.h"
+#include "qz_kernels.h"
+
+namespace qz {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return QZ_OK;
+  return fail(QZ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// SM count of the current device (cached per device).
+int current_sms(int* sms) {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(QZ_ERR_INVALID, "device index %d out of range", dev);
+  if (cache[dev] == 0) {
+    int major = 0, n = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (major != 10) return fail(QZ_ERR_UNSUPPORTED, "device %d is sm_%d0, this library targets sm_100a", dev, major);
+    cache[dev] = n;
+  }
+  *sms = cache[dev];
+  return QZ_OK;
+}
+
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}  // namespace qz
+
+using namespace qz;
+
+extern "C" {
+
+const char* qz_last_error(void) { return g_last_error.c_str(); }
+
+int qz_version(void) { return 100; }
+
+int qz_device_ok(void) {
+  int sms = 0;
+  return current_sms(&sms);
+}
+
+int qz_scale_table(int format, float* out_host, int* n_out) {
+  if (!out_host || !n_out) return fail(QZ_ERR_INVALID, "qz_scale_table: NULL output");
+  if (format == QZ_FMT_NVFP4) {
+    int n = 0;
+    for (int c = 1; c < 0x7f; ++c) {
+      int e = c >> 3, m = c & 7;
+      out_host[n++] = e == 0 ? (float)m / 512.0f : ldexpf(1.0f + m / 8.0f, e - 7);
+    }
+    *n_out = n;
+    return QZ_OK;
+  }
+  if (format == QZ_FMT_MXFP4) {
+    for (int e = 1; e <= 254; ++e) out_host[e - 1] = ldexpf(1.0f, e - 127);
+    *n_out = 254;
+    return QZ_OK;
+  }
+  return fail(QZ_ERR_INVALID, "qz_scale_table: unknown format %d", format);
+}
+
+int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, int format,
+                int method, const float* h_blocks, int64_t n_col_blocks, float* scales,
+                float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,
+                uint16_t* dq_bf16, void* stream) {
+  if (block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (format != QZ_FMT_NVFP4 && format != QZ_FMT_MXFP4)
+    return fail(QZ_ERR_INVALID, "unknown format %d", format);
+  if (method < QZ_METHOD_NAIVE || method > QZ_METHOD_TWO_ARGMIN)
+    return fail(QZ_ERR_INVALID, "unknown method %d", method);
+  if (x_dtype != QZ_DTYPE_F32 && x_dtype != QZ_DTYPE_BF16 && x_dtype != QZ_DTYPE_F16)
+    return fail(QZ_ERR_INVALID, "unknown dtype %d", x_dtype);
+  if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
+  if (n_blocks == 0) return QZ_OK;
+  if (!x) return fail(QZ_ERR_INVALID, "x is NULL");
+  if (!aligned(x, 16)) return fail(QZ_ERR_INVALID, "x must be 16-byte aligned");
+  if ((quants && !aligned(quants, 16)) || (dq && !aligned(dq, 16)) ||
+      (dq_bf16 && !aligned(dq_bf16, 16)) || (packed && !aligned(packed, block_size == 16 ? 8 : 16)))
+    return fail(QZ_ERR_INVALID, "quants/dq/dq_bf16 must be 16-byte aligned, packed 8/16-byte aligned");
+  if (method == QZ_METHOD_HESSIAN) {
+    if (!h_blocks) return fail(QZ_ERR_INVALID, "X or H_blocks required");
+    if (n_col_blocks <= 0 || n_blocks % n_col_blocks != 0)
+      return fail(QZ_ERR_INVALID, "n_blocks (%lld) must be a multiple of n_col_blocks (%lld)",
+                  (long long)n_blocks, (long long)n_col_blocks);
+    if (n_col_blocks > 2147483647LL) return fail(QZ_ERR_INVALID, "too many column blocks");
+    if (!aligned(h_blocks, 16)) return fail(QZ_ERR_INVALID, "h_blocks must be 16-byte aligned");
+  }
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  QuantArgs p{x, n_blocks, h_blocks, n_col_blocks, scales, quants, dq, scale_codes, packed, dq_bf16};
+  return cuda_status(launch_quantize(p, x_dtype, block_size, format, method, sms,
+                                     static_cast<cudaStream_t>(stream)),
+                     "qz_quantize launch");
+}
+
+int qz_dequantize(const float* scales, const float* quants, int64_t n_blocks, int block_size,
+                  float* out, void* stream) {
+  if (block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
+  if (n_blocks == 0) return QZ_OK;
+  if (!scales || !quants || !out) return fail(QZ_ERR_INVALID, "NULL pointer");
+  if (!aligned(quants, 16) || !aligned(out, 16))
+    return fail(QZ_ERR_INVALID, "quants and out must be 16-byte aligned");
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  return cuda_status(launch_dequantize(scales, quants, n_blocks, block_size, out, sms,
+                                       static_cast<cudaStream_t>(stream)),
+                     "qz_dequantize launch");
+}
+
+int qz_dequantize_packed(const uint8_t* packed, const uint8_t* scale_codes, int64_t n_blocks,
+                         int block_size, int format, float* out_f32, uint16_t* out_bf16,
+                         void* stream) {
+  if (block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (format != QZ_FMT_NVFP4 && format != QZ_FMT_MXFP4)
+    return fail(QZ_ERR_INVALID, "unknown format %d", format);
+  if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
+  if (n_blocks == 0) return QZ_OK;
+  if (!packed || !scale_codes) return fail(QZ_ERR_INVALID, "NULL input");
+  if (!aligned(packed, 4) || (out_f32 && !aligned(out_f32, 16)) || (out_bf16 && !aligned(out_bf16, 16)))
+    return fail(QZ_ERR_INVALID, "packed must be 4-byte aligned, outputs 16-byte aligned");
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  return cuda_status(launch_dequantize_packed(packed, scale_codes, n_blocks, block_size, format,
+                                              out_f32, out_bf16, sms,
+                                              static_cast<cudaStream_t>(stream)),
+                     "qz_dequantize_packed launch");
+}
+
+int qz_fp4_unpack(const uint8_t* packed, int64_t n_bytes, int8_t* out, void* stream) {
+  if (n_bytes < 0 || n_bytes % 4 != 0)
+    return fail(QZ_ERR_INVALID, "Input size must be a multiple of 4 bytes");
+  if (n_bytes == 0) return QZ_OK;
+  if (!packed || !out) return fail(QZ_ERR_INVALID, "NULL pointer");
+  if (!aligned(packed, 4) || !aligned(out, 8))
+    return fail(QZ_ERR_INVALID, "packed must be 4-byte aligned, out 8-byte aligned");
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  return cuda_status(launch_unpack(packed, n_bytes, out, sms, static_cast<cudaStream_t>(stream)),
+                     "qz_fp4_unpack launch");
+}
+
+int qz_weight_error_sums(const void* W, int w_dtype, const void* W_dq, int dq_dtype, int64_t n,
+                         double* sums, void* stream) {
+  if (w_dtype < 0 || w_dtype > 2 || dq_dtype < 0 || dq_dtype > 2)
+    return fail(QZ_ERR_INVALID, "unknown dtype");
+  if (n < 0) return fail(QZ_ERR_INVALID, "n must be >= 0");
+  if (n == 0) return QZ_OK;
+  if (!W || !W_dq || !sums) return fail(QZ_ERR_INVALID, "NULL pointer");
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  return cuda_status(launch_weight_sums(W, w_dtype, W_dq, dq_dtype, n, sums, sms,
+                                        static_cast<cudaStream_t>(stream)),
+                     "qz_weight_error_sums launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,169 @@
+// qz_common.cuh -- device helpers shared by the quantization kernels.
+//
+// The arithmetic restates the reference's pure-PyTorch CPU evaluation order
+// exactly (qwantize v0.1.2, nvfp4/reference.py and mxfp4/reference.py):
+//   * sum(-1) over a 16/32-element fp32 row = eight interleaved accumulators,
+//     acc[k] = v[k] + v[k+8] (+ v[k+16] + v[k+24]), then acc0 + acc1 + ... + acc7
+//     in sequence;
+//   * cumsum = sequential double accumulation, each prefix rounded to fp32;
+//   * every multiply / add / divide / sqrt is a separately rounded IEEE op
+//     (the translation units using this are compiled with -fmad=false and use
+//     the __f*_rn intrinsics).
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace qz {
+
+constexpr int kDtF32 = 0, kDtBF16 = 1, kDtF16 = 2;
+constexpr int kNVFP4 = 0, kMXFP4 = 1;
+constexpr int kNaive = 0, kSSE = 1, kHessian = 2, kNaiveArgmin = 3, kTwoArgmin = 4;
+
+// NaN bit patterns the reference produces for a NaN scale: the E4M3 NaN code
+// 0x7f widened to fp32 (NVFP4) and torch CPU log2/pow's all-ones NaN (MXFP4).
+constexpr uint32_t kNvNanBits = 0x7ff00000u;
+constexpr uint32_t kMxNanBits = 0xffffffffu;
+
+// E2M1 decision boundaries and codebook (nvfp4/reference.py:14-16).
+__device__ __forceinline__ constexpr float bnd(int k) {
+  return k == 0 ? 0.25f : k == 1 ? 0.75f : k == 2 ? 1.25f : k == 3 ? 1.75f
+       : k == 4 ? 2.5f : k == 5 ? 3.5f : 5.0f;
+}
+__device__ __forceinline__ constexpr float cbv(int k) {
+  return k == 0 ? 0.0f : k == 1 ? 0.5f : k == 2 ? 1.0f : k == 3 ? 1.5f
+       : k == 4 ? 2.0f : k == 5 ? 3.0f : k == 6 ? 4.0f : 6.0f;
+}
+
+__device__ __forceinline__ bool is_nan_bits(uint32_t abs_bits) { return abs_bits > 0x7f800000u; }
+
+// x.to(float8_e4m3fn).to(float32) for x >= 0 or NaN: round to nearest even,
+// subnormal step 2^-9, values above 464 (which round past 448) become NaN.
+__device__ __forceinline__ float e4m3_snap_nonneg(float a) {
+  if (!(a <= 464.0f)) return __uint_as_float(kNvNanBits);
+  if (a < 0.015625f) return __fmul_rn(rintf(__fmul_rn(a, 512.0f)), 0.001953125f);
+  uint32_t u = __float_as_uint(a);
+  u += 0x7ffffu + ((u >> 20) & 1u);
+  return __uint_as_float(u & 0xfff00000u);
+}
+
+// E4M3 code of a non-negative value on the E4M3 grid (NaN -> 0x7f).
+__device__ __forceinline__ uint32_t e4m3_code(float s) {
+  uint32_t u = __float_as_uint(s);
+  if (is_nan_bits(u & 0x7fffffffu)) return 0x7f;
+  if (s == 0.0f) return 0;
+  if (s < 0.015625f) return (uint32_t)__float2int_rn(__fmul_rn(s, 512.0f));
+  uint32_t e = ((u >> 23) & 0xff) - 120;
+  return (e << 3) | ((u >> 20) & 7);
+}
+
+// Value of positive E4M3 code c (1..126).
+__device__ __forceinline__ float e4m3_value(int c) {
+  if (c < 8) return __fmul_rn((float)c, 0.001953125f);
+  return __uint_as_float(((uint32_t)c << 20) + (120u << 23));
+}
+
+// Largest code whose value is <= v (0 if none); v >= 0 and not NaN.
+__device__ __forceinline__ int e4m3_floor_code(float v) {
+  if (v >= 448.0f) return 126;
+  if (v < 0.001953125f) return 0;
+  if (v < 0.015625f) return (int)floorf(__fmul_rn(v, 512.0f));
+  uint32_t u = __float_as_uint(v);
+  return (int)(((((u >> 23) & 0xff) - 120) << 3) | ((u >> 20) & 7));
+}
+
+// Smallest code whose value is >= v (127 if none); v >= 0 and not NaN.
+__device__ __forceinline__ int e4m3_ceil_code(float v) {
+  if (v <= 0.001953125f) return 1;
+  if (v > 448.0f) return 127;
+  int f = e4m3_floor_code(v);
+  return e4m3_value(f) == v ? f : f + 1;
+}
+
+// MXFP4 naive exponent (mxfp4/reference.py:114-118):
+// clamp(floor(log2(max(amax, 1e-30))) - 2 + 127, 1, 254), with the exact
+// floor(log2) from the bits (torch's fp32 log2 path gives the same for every
+// bf16/fp16 input).  NaN is handled by the caller.
+__device__ __forceinline__ int ue8m0_naive_exp(uint32_t amax_bits) {
+  if (amax_bits >= 0x7f800000u) return 254;   // inf
+  if (amax_bits < 0x0da24260u) return 25;     // below 1e-30f: log2(1e-30) = -99.66
+  int e = (int)(amax_bits >> 23) - 2;         // floor(log2) - 2 + 127
+  return e > 254 ? 254 : e;
+}
+
+__device__ __forceinline__ float pow2f(int e) {  // 2^e for -126 <= e <= 127
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
+// sum(-1) of a BS-element row in torch's CPU order.
+template <int BS>
+__device__ __forceinline__ float sum8(const float (&v)[BS]) {
+  float acc[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc[k] = v[k];
+#pragma unroll
+  for (int i = 8; i < BS; i += 8)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = __fadd_rn(acc[k], v[i + k]);
+  float r = acc[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) r = __fadd_rn(r, acc[k]);
+  return r;
+}
+
+// In-register ascending bitonic sort of non-negative float bit patterns
+// (NaN patterns sort last, like torch.sort).
+template <int N>
+__device__ __forceinline__ void bitonic_sort_u32(uint32_t (&v)[N]) {
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        int l = i ^ j;
+        if (l > i) {
+          uint32_t a = v[i], b = v[l];
+          uint32_t lo = min(a, b), hi = max(a, b);
+          if ((i & k) == 0) { v[i] = lo; v[l] = hi; }
+          else { v[i] = hi; v[l] = lo; }
+        }
+      }
+    }
+  }
+}
+
+template <int DT>
+struct Elem { static constexpr int kSize = DT == kDtF32 ? 4 : 2; };
+
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t h) { return __uint_as_float(h << 16); }
+__device__ __forceinline__ float f16_bits_to_float(uint32_t h) {
+  return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+// Load one block of BS elements (16-byte aligned) as fp32.
+template <int BS, int DT>
+__device__ __forceinline__ void load_block(const void* base, int64_t blk, float (&x)[BS]) {
+  const uint4* p = reinterpret_cast<const uint4*>(
+      static_cast<const char*>(base) + blk * (int64_t)(BS * Elem<DT>::kSize));
+  constexpr int kVec = BS * Elem<DT>::kSize / 16;
+#pragma unroll
+  for (int v = 0; v < kVec; ++v) {
+    uint4 w = __ldg(p + v);
+    uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (DT == kDtF32) {
+        x[v * 4 + k] = __uint_as_float(ww[k]);
+      } else if (DT == kDtBF16) {
+        x[v * 8 + 2 * k] = bf16_bits_to_float(ww[k] & 0xffffu);
+        x[v * 8 + 2 * k + 1] = bf16_bits_to_float(ww[k] >> 16);
+      } else {
+        x[v * 8 + 2 * k] = f16_bits_to_float(ww[k] & 0xffffu);
+        x[v * 8 + 2 * k + 1] = f16_bits_to_float(ww[k] >> 16);
+      }
+    }
+  }
+}
+
+}  // namespace qz

@@ -1,0 +1,185 @@
+// qz_elementwise.cu -- HBM-bound kernels: dequantize (fp32 and packed storage),
+// fp4 nibble unpack, and the weight-error sums of compute_metrics.
+// Grid-stride loops over 16-byte vectors, grids sized to a multiple of the SM
+// count.
+#include "qz_common.cuh"
+#include "qz_kernels.h"
+
+namespace qz {
+
+// quants * scales with x86 NaN payload propagation (first NaN operand, quieted),
+// which is what the reference's CPU `quants * scales.unsqueeze(dim)` returns.
+__device__ __forceinline__ float mul_x86(float q, float s) {
+  float r = __fmul_rn(q, s);
+  if (r != r) {
+    uint32_t qb = __float_as_uint(q), sb = __float_as_uint(s);
+    if (is_nan_bits(qb & 0x7fffffffu)) return __uint_as_float(qb | 0x00400000u);
+    if (is_nan_bits(sb & 0x7fffffffu)) return __uint_as_float(sb | 0x00400000u);
+    return __uint_as_float(0xffc00000u);  // inf * 0: x86 default NaN
+  }
+  return r;
+}
+
+// nvfp4/reference.py:537-549, blocked layout; one float4 per thread step.
+__global__ void dequantize_kernel(const float* __restrict__ scales, const float4* __restrict__ q,
+                                  int64_t n_vec, int shift_vec_per_block, float4* __restrict__ out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_vec; i += stride) {
+    float s = __ldg(scales + (i >> shift_vec_per_block));
+    float4 v = __ldg(q + i);
+    out[i] = make_float4(mul_x86(v.x, s), mul_x86(v.y, s), mul_x86(v.z, s), mul_x86(v.w, s));
+  }
+}
+
+__device__ __forceinline__ float e2m1_value(uint32_t nib) {
+  float m = cbv((int)(nib & 7u));
+  return (nib & 8u) ? -m : m;
+}
+
+__device__ __forceinline__ float code_to_scale(uint32_t c, int fmt) {
+  if (fmt == kNVFP4) {
+    uint32_t m = c & 0x7fu;
+    if (m == 0x7fu) return __uint_as_float(kNvNanBits);
+    float v = m == 0 ? 0.0f : e4m3_value((int)m);
+    return (c & 0x80u) ? -v : v;
+  }
+  if (c == 0xffu) return __uint_as_float(kMxNanBits);
+  if (c == 0) return __uint_as_float(0x00400000u);  // 2^-127 (subnormal fp32)
+  return pow2f((int)c - 127);
+}
+
+// One thread per 8 elements (4 packed bytes).
+__global__ void dequantize_packed_kernel(const uint32_t* __restrict__ packed,
+                                         const uint8_t* __restrict__ codes, int64_t n_words,
+                                         int words_per_block_shift, int fmt,
+                                         float4* __restrict__ out_f32, uint4* __restrict__ out_bf16) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words; i += stride) {
+    float s = code_to_scale(__ldg(codes + (i >> words_per_block_shift)), fmt);
+    uint32_t w = __ldg(packed + i);
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float q = e2m1_value((w >> (4 * k)) & 0xfu);
+      v[k] = (s != s) ? s : __fmul_rn(q, s);
+    }
+    if (out_f32) {
+      out_f32[2 * i] = make_float4(v[0], v[1], v[2], v[3]);
+      out_f32[2 * i + 1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    if (out_bf16) {
+      uint32_t h[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        h[k] = (__float_as_uint(v[2 * k]) >> 16) | (__float_as_uint(v[2 * k + 1]) & 0xffff0000u);
+      out_bf16[i] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+}
+
+// fp4.py:117-254: nibble bits 0-2 index {0,1,2,3,4,6,8,12}, bit 3 = sign.
+__global__ void unpack_kernel(const uint32_t* __restrict__ in, int64_t n_words,
+                              uint2* __restrict__ out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words; i += stride) {
+    uint32_t w = __ldg(in + i), o[2] = {0, 0};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t nib = (w >> (4 * k)) & 0xfu;
+      uint32_t mag = (0xC8643210u >> (4 * (nib & 7u))) & 0xfu;
+      uint32_t v = (nib & 8u) ? ((0u - mag) & 0xffu) : mag;
+      o[k >> 2] |= v << (8 * (k & 3));
+    }
+    out[i] = make_uint2(o[0], o[1]);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ float load1(const void* p, int64_t i) {
+  if (DT == kDtF32) return __ldg(static_cast<const float*>(p) + i);
+  uint32_t h = __ldg(static_cast<const unsigned short*>(p) + i);
+  return DT == kDtBF16 ? bf16_bits_to_float(h) : f16_bits_to_float(h);
+}
+
+// sums[0] += sum (dq - w)^2, sums[1] += sum w^2 (double), metrics.py:23-27.
+template <int WDT, int DDT>
+__global__ void weight_sums_kernel(const void* __restrict__ W, const void* __restrict__ Wdq, int64_t n,
+                                   double* __restrict__ sums) {
+  double e = 0.0, w2 = 0.0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    double w = load1<WDT>(W, i), d = (double)load1<DDT>(Wdq, i) - w;
+    e += d * d;
+    w2 += w * w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    e += __shfl_xor_sync(0xffffffffu, e, o);
+    w2 += __shfl_xor_sync(0xffffffffu, w2, o);
+  }
+  __shared__ double red[2][32];
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) { red[0][wid] = e; red[1][wid] = w2; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0, b = 0;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) { a += red[0][k]; b += red[1][k]; }
+    atomicAdd(sums, a);
+    atomicAdd(sums + 1, b);
+  }
+}
+
+static unsigned grid_for(int64_t n_items, int threads, int num_sms, int per_sm = 8) {
+  int64_t g = (n_items + threads - 1) / threads, cap = (int64_t)num_sms * per_sm;
+  return (unsigned)(g < cap ? (g < 1 ? 1 : g) : cap);
+}
+
+cudaError_t launch_dequantize(const float* scales, const float* quants, int64_t n_blocks, int bs,
+                              float* out, int num_sms, cudaStream_t st) {
+  int64_t n_vec = n_blocks * bs / 4;
+  if (n_vec == 0) return cudaSuccess;
+  dequantize_kernel<<<grid_for(n_vec, 256, num_sms), 256, 0, st>>>(
+      scales, reinterpret_cast<const float4*>(quants), n_vec, bs == 16 ? 2 : 3,
+      reinterpret_cast<float4*>(out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize_packed(const uint8_t* packed, const uint8_t* codes, int64_t n_blocks,
+                                     int bs, int fmt, float* out_f32, uint16_t* out_bf16,
+                                     int num_sms, cudaStream_t st) {
+  int64_t n_words = n_blocks * bs / 8;
+  if (n_words == 0) return cudaSuccess;
+  dequantize_packed_kernel<<<grid_for(n_words, 256, num_sms), 256, 0, st>>>(
+      reinterpret_cast<const uint32_t*>(packed), codes, n_words, bs == 16 ? 1 : 2, fmt,
+      reinterpret_cast<float4*>(out_f32), reinterpret_cast<uint4*>(out_bf16));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_unpack(const uint8_t* packed, int64_t n_bytes, int8_t* out, int num_sms,
+                          cudaStream_t st) {
+  int64_t n_words = n_bytes / 4;
+  if (n_words == 0) return cudaSuccess;
+  unpack_kernel<<<grid_for(n_words, 256, num_sms), 256, 0, st>>>(
+      reinterpret_cast<const uint32_t*>(packed), n_words, reinterpret_cast<uint2*>(out));
+  return cudaGetLastError();
+}
+
+template <int WDT>
+static void launch_ws(const void* W, const void* Wdq, int ddt, int64_t n, double* sums,
+                      unsigned g, cudaStream_t st) {
+  if (ddt == kDtF32) weight_sums_kernel<WDT, kDtF32><<<g, 256, 0, st>>>(W, Wdq, n, sums);
+  else if (ddt == kDtBF16) weight_sums_kernel<WDT, kDtBF16><<<g, 256, 0, st>>>(W, Wdq, n, sums);
+  else weight_sums_kernel<WDT, kDtF16><<<g, 256, 0, st>>>(W, Wdq, n, sums);
+}
+
+cudaError_t launch_weight_sums(const void* W, int wdt, const void* Wdq, int ddt, int64_t n,
+                               double* sums, int num_sms, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  unsigned g = grid_for(n, 256, num_sms, 4);
+  if (wdt == kDtF32) launch_ws<kDtF32>(W, Wdq, ddt, n, sums, g, st);
+  else if (wdt == kDtBF16) launch_ws<kDtBF16>(W, Wdq, ddt, n, sums, g, st);
+  else launch_ws<kDtF16>(W, Wdq, ddt, n, sums, g, st);
+  return cudaGetLastError();
+}
+
+}  // namespace qz

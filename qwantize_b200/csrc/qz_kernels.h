@@ -1,0 +1,34 @@
+// qz_kernels.h -- internal launch interface between the C ABI (qz_abi.cu) and
+// the kernel translation units.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qz {
+
+struct QuantArgs {
+  const void* x;
+  int64_t n_blocks;
+  const float* h_blocks;
+  int64_t n_col_blocks;
+  float* scales;
+  float* quants;
+  float* dq;
+  uint8_t* scale_codes;
+  uint8_t* packed;
+  uint16_t* dq_bf16;
+};
+
+cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int method,
+                            int num_sms, cudaStream_t st);
+cudaError_t launch_dequantize(const float* scales, const float* quants, int64_t n_blocks, int bs,
+                              float* out, int num_sms, cudaStream_t st);
+cudaError_t launch_dequantize_packed(const uint8_t* packed, const uint8_t* codes, int64_t n_blocks,
+                                     int bs, int fmt, float* out_f32, uint16_t* out_bf16,
+                                     int num_sms, cudaStream_t st);
+cudaError_t launch_unpack(const uint8_t* packed, int64_t n_bytes, int8_t* out, int num_sms,
+                          cudaStream_t st);
+cudaError_t launch_weight_sums(const void* W, int wdt, const void* Wdq, int ddt, int64_t n,
+                               double* sums, int num_sms, cudaStream_t st);
+
+}  // namespace qz

@@ -1,0 +1,49 @@
+"""Block Hessians H_j = X_j^T X_j for the Hessian-weighted scale search.
+
+Replaces the reference's Python double loop of fp32 ``addmm_`` calls
+(nvfp4/reference.py:304-317) with the tcgen05 Gram kernel (qz_gram)."""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from .core import cuda_device
+
+
+def gram(X: torch.Tensor, mode: str = "full", block_size: int = 16, out: torch.Tensor = None,
+         accumulate: bool = False) -> torch.Tensor:
+    """H = X^T X in fp32 for bf16 X (T, K).  mode "full" -> (K, K);
+    "blockdiag" -> (K/bs, bs, bs)."""
+    assert X.ndim == 2
+    dev = cuda_device(X)
+    Xd = X.to(dev, torch.bfloat16).contiguous()
+    T, K = Xd.shape
+    m = L.GRAM_FULL if mode == "full" else L.GRAM_BLOCKDIAG
+    if m == L.GRAM_BLOCKDIAG:
+        assert K % block_size == 0
+        shape = (K // block_size, block_size, block_size)
+    else:
+        shape = (K, K)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=dev)
+        accumulate = False
+    assert tuple(out.shape) == shape and out.dtype == torch.float32 and out.is_contiguous()
+    L.check(L.load().qz_gram(L.ptr(Xd), T, K, m, block_size, int(accumulate), L.ptr(out),
+                             L.stream_ptr(dev)), "qz_gram")
+    return out
+
+
+def block_hessians(X: torch.Tensor, block_size: int) -> torch.Tensor:
+    return gram(X, "blockdiag", block_size)
+
+
+def resolve_h_blocks(W: torch.Tensor, dim: int, X, H_blocks) -> torch.Tensor:
+    """The (J, bs, bs) fp32 device tensor the search uses: H_blocks if given
+    (X is then ignored, as in the reference), else built from X."""
+    assert X is not None or H_blocks is not None, "X or H_blocks required"
+    bs = W.shape[dim % W.ndim]
+    assert bs in (16, 32)
+    dev = cuda_device(W)
+    if H_blocks is not None:
+        return H_blocks.to(dev, torch.float32).contiguous()
+    return block_hessians(X, bs)
