@@ -136,6 +136,15 @@ QZ_API int qz_weight_error_sums(const void* W, int w_dtype, const void* W_dq, in
 QZ_API int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, const uint16_t* W,
                          const uint16_t* W_dq, int64_t M, double* sums, void* stream);
 
+/*
+ * qz_poll_device_error -- reads (and with clear != 0 resets) the flags that
+ * bounded device-side waits set when they give up (bit 0: bulk-load wait,
+ * bit 1: tensor-core pipeline wait, bit 2: epilogue wait).  Synchronous.
+ * Returns QZ_ERR_TIMEOUT if any flag was set.  (No counterpart in the
+ * reference, whose kernels have no device-side waits.)
+ */
+QZ_API int qz_poll_device_error(int clear, unsigned* flags_out);
+
 /* Host helpers. */
 QZ_API int qz_scale_table(int format, float* out_host, int* n_out); /* 126 / 254 ascending values */
 QZ_API const char* qz_last_error(void);

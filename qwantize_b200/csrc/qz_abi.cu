@@ -56,6 +56,15 @@ const char* qz_last_error(void) { return g_last_error.c_str(); }
 
 int qz_version(void) { return 100; }
 
+int qz_poll_device_error(int clear, unsigned* flags_out) {
+  unsigned f = 0;
+  int st = cuda_status(read_device_error_quantize(&f, clear != 0), "qz_poll_device_error");
+  if (flags_out) *flags_out = f;
+  if (st != QZ_OK) return st;
+  if (f) return fail(QZ_ERR_TIMEOUT, "a device-side wait gave up (flags 0x%x)", f);
+  return QZ_OK;
+}
+
 int qz_device_ok(void) {
   int sms = 0;
   return current_sms(&sms);

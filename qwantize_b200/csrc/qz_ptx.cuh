@@ -1,0 +1,87 @@
+// qz_ptx.cuh -- thin inline-PTX wrappers for sm_100a: mbarriers, bulk (TMA)
+// copies, fences and bounded waits.  Every wait gives up after kWaitLimitNs,
+// records an error code in qz_device_error and returns false, so a kernel can
+// never spin forever.
+#pragma once
+#include <cstdint>
+
+namespace qz {
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Error codes recorded in the device flag (bitwise OR of all that occurred).
+constexpr unsigned kDevErrLoadTimeout = 1u;
+constexpr unsigned kDevErrMmaTimeout = 2u;
+constexpr unsigned kDevErrEpilogueTimeout = 4u;
+
+// One flag per translation unit (internal linkage: the library is compiled
+// without relocatable device code); each unit exports a host reader.
+static __device__ unsigned qz_device_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (TMA / tensor core) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete; false (and the error flag set)
+// if it did not within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&qz_device_error, err);
+      return false;
+    }
+  }
+  return true;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes and both
+// addresses 16-byte aligned; no multicast).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace qz

@@ -1,9 +1,24 @@
 // qz_quantize.cu -- fused per-block scale search + E2M1 quantization for sm_100a.
 //
-// One thread owns one block of 16/32 elements (a block is 32-128 contiguous
-// bytes, read with 128-bit loads), computes amax, the naive scale, and for the
-// search methods the reference's bounds and candidate loop, then writes every
-// requested output in the same pass.  Semantics follow qwantize v0.1.2:
+// Layout of the work.  Blocks (16 or 32 contiguous elements) are grouped in
+// chunks of 32, one chunk per warp at a time.  Every warp runs its own bulk-copy
+// (TMA) pipeline: lane 0 keeps kStages chunk loads in flight into the warp's
+// shared-memory ring, completion tracked by one mbarrier per stage, so HBM reads
+// are large contiguous transfers and warps never wait for each other.
+//   * Lane L owns block L of the chunk: amax, naive scale, search bounds, final
+//     quantization and all stores of that block.
+//   * SSE search: the (block, candidate) pairs of the whole chunk are spread
+//     evenly over the 32 lanes (a block's candidates are data dependent, 0..39),
+//     each lane evaluates its pairs against |x| rows kept in shared memory, and
+//     the winner per block is the minimum of the 64-bit key (SSE bits, index).
+//     This equals the reference's ascending loop with strict '<' updates: the
+//     first (lowest) scale achieving the minimum SSE, kept only if below the
+//     naive error.  (The reference's clipping fast-fail never changes that
+//     winner: a candidate's clipping error is a partial sum, in the same order,
+//     of its SSE's non-negative terms.)
+//   * Hessian search keeps the reference's sequential semantics (its fast-fail
+//     does change results) in a CTA-per-column-block kernel with H_j in smem.
+// Semantics follow qwantize v0.1.2:
 //   naive   nvfp4/reference.py:89-126, mxfp4/reference.py:89-129
 //   SSE     nvfp4/reference.py:129-239, mxfp4/reference.py:132-238
 //   Hessian nvfp4/reference.py:266-407, mxfp4/reference.py:241-374 (the shipped
@@ -13,41 +28,65 @@
 // the order torch's CPU kernels use, so results are bit-identical.
 #include "qz_common.cuh"
 #include "qz_kernels.h"
+#include "qz_ptx.cuh"
 
 namespace qz {
 
-// Fast E2M1 dequant magnitude t = q*s of a = |x| for a finite s >= 0.
-// For bf16/fp16 inputs the division-free compare a > B_k*s is exactly
-// bucketize(a/s) (a has <= 11 significant bits, B_k*s <= 7, so a/s can only
-// round onto a boundary when it equals it); fp32 inputs use the IEEE quotient.
-template <int DT>
+// How bucketize(|x| / s) is evaluated exactly:
+//   NVFP4, bf16/fp16 input: count thresholds B_k*s that |x| exceeds (|x| has
+//     <= 11 significant bits and B_k*s <= 7, so |x|/s rounds onto a boundary
+//     only when it equals it; B_k*s <= 5*448 never overflows);
+//   NVFP4, fp32 input: the IEEE quotient;
+//   MXFP4: |x| times the exact reciprocal 2^-e (identical to the quotient).
+enum RoundMode { kCmp = 0, kDiv = 1, kRcp = 2 };
+template <int FMT, int DT>
+struct Mode { static constexpr int v = FMT == kMXFP4 ? kRcp : (DT == kDtF32 ? kDiv : kCmp); };
+
+// Dequant magnitude t = q*s for a = |x| and a finite scale s >= 0.
+template <int MODE>
 struct FastQ {
-  float T[7], V[7], s;
+  float T[7], V[7], s, r;
   __device__ __forceinline__ explicit FastQ(float s_) : s(s_) {
 #pragma unroll
     for (int k = 0; k < 7; ++k) {
-      T[k] = __fmul_rn(bnd(k), s_);
+      if (MODE == kCmp) T[k] = __fmul_rn(bnd(k), s_);
       V[k] = __fmul_rn(cbv(k + 1), s_);
     }
+    r = MODE == kRcp ? __frcp_rn(s_) : 0.0f;
   }
   __device__ __forceinline__ float operator()(float a) const {
     float t = 0.0f;
-    if (DT == kDtF32) {
-      float y = __fdiv_rn(a, s);
-#pragma unroll
-      for (int k = 0; k < 7; ++k) t = (y > bnd(k)) ? V[k] : t;
-    } else {
+    if (MODE == kCmp) {
 #pragma unroll
       for (int k = 0; k < 7; ++k) t = (a > T[k]) ? V[k] : t;
+    } else {
+      float y = MODE == kDiv ? __fdiv_rn(a, s) : __fmul_rn(a, r);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) t = (y > bnd(k)) ? V[k] : t;
     }
     return t;
   }
 };
 
+// bucketize index for any scale (0, NaN included): #{k : !(y <= B_k)}.
+template <int MODE>
+__device__ __forceinline__ int fp4_index(float a, float s) {
+  int idx = 0;
+  if (MODE == kCmp) {
+#pragma unroll
+    for (int k = 0; k < 7; ++k) idx += (a <= __fmul_rn(bnd(k), s)) ? 0 : 1;
+  } else {
+    float y = MODE == kDiv ? __fdiv_rn(a, s) : __fmul_rn(a, __frcp_rn(s));
+#pragma unroll
+    for (int k = 0; k < 7; ++k) idx += (y <= bnd(k)) ? 0 : 1;
+  }
+  return idx;
+}
+
 // Block SSE (compute_block_sse, nvfp4/reference.py:72-86) for finite s >= 0.
-template <int BS, int DT>
+template <int BS, int MODE>
 __device__ __forceinline__ float block_sse(const float (&a)[BS], float s) {
-  FastQ<DT> q(s);
+  FastQ<MODE> q(s);
   float d2[BS];
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
@@ -70,21 +109,21 @@ __device__ __forceinline__ float block_clip(const float (&a)[BS], float s) {
   return sum8<BS>(v);
 }
 
-// r^T H r with r = x - dq: Hr_a = fma-chain over b ascending, then the torch
-// sum order over r_a * Hr_a.  Hj points at shared memory (all threads of the
-// CTA read the same H_j: broadcast).
-template <int BS, int DT>
+// r^T H r with r = x - dq: Hr_a = fma chain over b ascending, then the torch
+// sum order over r_a * Hr_a.  Hj is in shared memory (broadcast reads).
+template <int BS, int MODE>
 __device__ __forceinline__ float block_hess(const float (&x)[BS], const float (&a)[BS], float s,
                                             const float* __restrict__ Hj) {
-  FastQ<DT> q(s);
-  float r[BS], p[BS];
+  FastQ<MODE> q(s);
+  float r[BS];
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
     float t = q(a[i]);
     float dq = x[i] > 0.0f ? t : (x[i] < 0.0f ? -t : 0.0f);
     r[i] = __fsub_rn(x[i], dq);
   }
-#pragma unroll
+  float acc8[8];
+#pragma unroll 1
   for (int ra = 0; ra < BS; ++ra) {
     const float4* h4 = reinterpret_cast<const float4*>(Hj + ra * BS);
     float acc = 0.0f;
@@ -96,9 +135,21 @@ __device__ __forceinline__ float block_hess(const float (&x)[BS], const float (&
       acc = __fmaf_rn(h.z, r[4 * b4 + 2], acc);
       acc = __fmaf_rn(h.w, r[4 * b4 + 3], acc);
     }
-    p[ra] = __fmul_rn(r[ra], acc);
+    // r[ra] with a runtime index would spill r to local memory: select instead
+    float rr = 0.0f;
+#pragma unroll
+    for (int i = 0; i < BS; ++i) rr = (i == ra) ? r[i] : rr;
+    float pa = __fmul_rn(rr, acc);
+    // torch sum order: acc8[k] = p[k] + p[k+8] (+ p[k+16] + p[k+24])
+    int k = ra & 7;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j == k) acc8[j] = ra < 8 ? pa : __fadd_rn(acc8[j], pa);
   }
-  return sum8<BS>(p);
+  float res = acc8[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) res = __fadd_rn(res, acc8[k]);
+  return res;
 }
 
 // Naive scale for FMT from amax bits (NaN propagates with the reference's bits).
@@ -114,9 +165,9 @@ __device__ __forceinline__ float naive_scale(uint32_t amax_bits) {
   return pow2f(ue8m0_naive_exp(amax_bits) - 127);
 }
 
-// Bounds of the bounded search (nvfp4/reference.py:171-189).  Returns the
-// inclusive range [lo, hi] of candidate indices (codes for NVFP4, biased
-// exponents for MXFP4); lo > hi when there is nothing to search.
+// Bounds of the bounded search (nvfp4/reference.py:171-189).  Produces the
+// inclusive range [lo, hi] of candidate indices (E4M3 codes / UE8M0 biased
+// exponents); lo > hi when there is nothing to search.
 template <int BS, int FMT>
 __device__ __forceinline__ void search_range(const float (&x)[BS], const float (&a)[BS],
                                              float amax, float E0, int& lo, int& hi) {
@@ -164,19 +215,23 @@ __device__ __forceinline__ float cand_value(int c) {
   return FMT == kNVFP4 ? e4m3_value(c) : pow2f(c - 127);
 }
 
-// Signed codebook entries of mxfp4/kernels.py:284-287.
+// Signed codebook of mxfp4/kernels.py:284-287 (entry 8 is +0.0).
 __device__ __forceinline__ float cb16(int k) { return k < 8 ? cbv(k) : (k == 8 ? 0.0f : -cbv(k - 8)); }
 
-// argmin_k |x - s*cb16[k]| with torch.argmin semantics (first NaN wins, else
-// first minimum); returns the index k.
+// argmin_k |x - s*cb16[k]| with torch.argmin semantics (the first NaN wins,
+// else the first minimum).
 __device__ __forceinline__ int argmin_index(float x, float s) {
   int best = 0;
   float bd = 0.0f;
-#pragma unroll 1
+  bool found_nan = false;
+#pragma unroll
   for (int k = 0; k < 16; ++k) {
     float d = fabsf(__fsub_rn(x, __fmul_rn(s, cb16(k))));
-    if (d != d) { best = k; break; }
-    if (k == 0 || d < bd) { bd = d; best = k; }
+    bool isn = d != d;
+    if (!found_nan) {
+      if (isn) { best = k; found_nan = true; }
+      else if (k == 0 || d < bd) { bd = d; best = k; }
+    }
   }
   return best;
 }
@@ -194,8 +249,8 @@ __device__ __forceinline__ float block_sse_argmin(const float (&x)[BS], float s)
 
 // Final quantization with scale s (any value, NaN included) and all outputs.
 template <int BS, int FMT, int METHOD, int DT>
-__device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const float (&x)[BS],
-                                            const float (&a)[BS], float s) {
+__device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const float (&x)[BS], float s) {
+  constexpr int MODE = Mode<FMT, DT>::v;
   float quant[BS];
   uint32_t nib[BS];
   const bool argmin = METHOD == kNaiveArgmin || METHOD == kTwoArgmin;
@@ -206,15 +261,7 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
       quant[i] = cb16(k);
       nib[i] = k < 8 ? k : (k == 8 ? 0 : 8 + (k - 8));
     } else {
-      int idx = 0;
-      if (DT == kDtF32) {
-        float y = __fdiv_rn(a[i], s);
-#pragma unroll
-        for (int k = 0; k < 7; ++k) idx += (y <= bnd(k)) ? 0 : 1;
-      } else {
-#pragma unroll
-        for (int k = 0; k < 7; ++k) idx += (a[i] <= __fmul_rn(bnd(k), s)) ? 0 : 1;
-      }
+      int idx = fp4_index<MODE>(fabsf(x[i]), s);
       float q = cbv(idx);
       quant[i] = x[i] > 0.0f ? q : (x[i] < 0.0f ? -q : 0.0f);  // torch.sign semantics
       nib[i] = (x[i] < 0.0f ? 8u : 0u) | ((x[i] > 0.0f || x[i] < 0.0f) ? (uint32_t)idx : 0u);
@@ -277,51 +324,175 @@ __device__ __forceinline__ uint32_t abs_and_amax(const float (&x)[BS], float (&a
   for (int i = 0; i < BS; ++i) {
     uint32_t u = __float_as_uint(x[i]) & 0x7fffffffu;
     a[i] = __uint_as_float(u);
-    m = max(m, u);  // NaN patterns compare above inf: NaN propagates like amax
+    m = max(m, u);  // NaN patterns compare above inf: NaN propagates like torch amax
   }
   return m;
 }
 
-// Naive / SSE / argmin methods: grid-stride, one thread per block.
+// Convert one block from raw shared memory to fp32.
+template <int BS, int DT>
+__device__ __forceinline__ void smem_block(const unsigned char* raw, float (&x)[BS]) {
+  const uint4* p = reinterpret_cast<const uint4*>(raw);
+  constexpr int kVec = BS * Elem<DT>::kSize / 16;
+#pragma unroll
+  for (int v = 0; v < kVec; ++v) {
+    uint4 w = p[v];
+    uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (DT == kDtF32) {
+        x[v * 4 + k] = __uint_as_float(ww[k]);
+      } else if (DT == kDtBF16) {
+        x[v * 8 + 2 * k] = bf16_bits_to_float(ww[k] & 0xffffu);
+        x[v * 8 + 2 * k + 1] = bf16_bits_to_float(ww[k] >> 16);
+      } else {
+        x[v * 8 + 2 * k] = f16_bits_to_float(ww[k] & 0xffffu);
+        x[v * 8 + 2 * k + 1] = f16_bits_to_float(ww[k] >> 16);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-warp geometry
+// ---------------------------------------------------------------------------
+constexpr int kWarps = 8;             // warps per CTA
+constexpr int kThreads = kWarps * 32;
+
+template <int BS, int DT, int METHOD>
+struct WarpGeom {
+  static constexpr int kChunkBytes = 32 * BS * Elem<DT>::kSize;  // 1-4 KB
+  static constexpr int kStages = kChunkBytes <= 2048 ? 4 : 2;
+  static constexpr bool kCoop = METHOD == kSSE;
+  static constexpr int kRowBytes = kCoop ? 32 * BS * 4 : 0;     // |x| rows for cooperation
+  static constexpr int kBytes = kStages * kChunkBytes + kRowBytes + (kCoop ? 32 * 8 + 64 * 4 : 0) +
+                                kStages * 8;
+  static constexpr int kBytesAligned = (kBytes + 127) / 128 * 128;
+};
+
+// Naive / SSE / argmin methods.
 template <int BS, int FMT, int METHOD, int DT>
-__global__ void __launch_bounds__(256) quantize_kernel(QuantArgs p) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < p.n_blocks; b += stride) {
-    float x[BS], a[BS];
-    load_block<BS, DT>(p.x, b, x);
+__global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
+  using G = WarpGeom<BS, DT, METHOD>;
+  constexpr int MODE = Mode<FMT, DT>::v;
+  constexpr int S = G::kStages;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned char* wbase = smem_raw + warp * G::kBytesAligned;
+  unsigned char* stage = wbase;                                  // S x chunk
+  float* rows = reinterpret_cast<float*>(wbase + S * G::kChunkBytes);  // 32 x BS |x|
+  unsigned long long* best = reinterpret_cast<unsigned long long*>(
+      wbase + S * G::kChunkBytes + G::kRowBytes);                 // 32 keys
+  int* incl = reinterpret_cast<int*>(best + (G::kCoop ? 32 : 0)); // 32 inclusive sums
+  int* lo_s = incl + (G::kCoop ? 32 : 0);                         // 32 lows
+  uint64_t* bar = reinterpret_cast<uint64_t*>(
+      wbase + S * G::kChunkBytes + G::kRowBytes + (G::kCoop ? 32 * 8 + 64 * 4 : 0));
+
+  const int64_t n_chunks = (p.n_blocks + 31) / 32;
+  const int64_t gwarp = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const char* src = static_cast<const char*>(p.x);
+
+  auto issue = [&](int64_t i) {  // lane 0 only
+    int64_t ch = gwarp + i * nwarps;
+    if (ch >= n_chunks) return;
+    int64_t nb = p.n_blocks - ch * 32;
+    nb = nb < 32 ? nb : 32;
+    uint32_t bytes = (uint32_t)(nb * BS * Elem<DT>::kSize);
+    uint64_t* b = bar + (i % S);
+    mbar_arrive_expect_tx(b, bytes);
+    bulk_load(stage + (i % S) * G::kChunkBytes, src + ch * (int64_t)G::kChunkBytes, bytes, b);
+  };
+
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(bar + s, 1);
+    fence_barrier_init();
+    for (int s = 0; s < S; ++s) issue(s);
+  }
+  __syncwarp();
+
+  for (int64_t i = 0;; ++i) {
+    const int64_t ch = gwarp + i * nwarps;
+    if (ch >= n_chunks) break;
+    if (!mbar_wait_bounded(bar + (i % S), (uint32_t)((i / S) & 1), kDevErrLoadTimeout)) return;
+    const int64_t blk = ch * 32 + lane;
+    const bool valid = blk < p.n_blocks;
+    float x[BS];
+    if (valid) smem_block<BS, DT>(stage + (i % S) * G::kChunkBytes + lane * BS * Elem<DT>::kSize, x);
+    else {
+#pragma unroll
+      for (int k = 0; k < BS; ++k) x[k] = 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      fence_proxy_async_smem();
+      issue(i + S);
+    }
+
+    float a[BS];
     uint32_t amax_bits = abs_and_amax<BS>(x, a);
     float s = naive_scale<FMT>(amax_bits);
-    // A NaN naive scale (NaN amax, or NVFP4 amax/6 > 464) makes the reference's
-    // E0 and bounds NaN, so no candidate is ever in range: keep it.
     const bool s_nan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
-    if (METHOD == kSSE && !s_nan) {
-      float E0 = block_sse<BS, DT>(a, s);
-      int lo, hi;
-      search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
-      // The reference skips a candidate whose clipping error is not below the
-      // running best; that error never exceeds the candidate's SSE (same terms,
-      // same order, the rest non-negative), so skipping it cannot change which
-      // candidate wins a strict '<' update -- it is omitted here.
-      float best_E = E0;
-#pragma unroll 1
-      for (int c = lo; c <= hi; ++c) {
-        float sc = cand_value<FMT>(c);
-        float E = block_sse<BS, DT>(a, sc);
-        if (E < best_E) { best_E = E; s = sc; }
+
+    if constexpr (METHOD == kSSE) {
+      // A NaN naive scale (NaN amax, or NVFP4 amax/6 > 464) makes the
+      // reference's E0 and bounds NaN: no candidate is ever in range.
+      int lo = 1, hi = 0;
+      float E0 = 0.0f;
+      if (valid && !s_nan) {
+        E0 = block_sse<BS, MODE>(a, s);
+        search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
       }
-    } else if (METHOD == kTwoArgmin && !is_nan_bits(amax_bits)) {
-      int e0 = ue8m0_naive_exp(amax_bits);
-      int e1 = e0 + 1 > 254 ? 254 : e0 + 1;
-      float s1 = pow2f(e1 - 127);
-      if (block_sse_argmin<BS>(x, s1) < block_sse_argmin<BS>(x, s)) s = s1;
+      const int n = hi >= lo ? hi - lo + 1 : 0;
+      float4* row = reinterpret_cast<float4*>(rows + lane * BS);
+#pragma unroll
+      for (int v = 0; v < BS / 4; ++v) row[v] = make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
+      int sc = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(0xffffffffu, sc, o);
+        if (lane >= o) sc += t;
+      }
+      incl[lane] = sc;
+      lo_s[lane] = lo;
+      best[lane] = (unsigned long long)__float_as_uint(E0) << 32;
+      const int total = __shfl_sync(0xffffffffu, sc, 31);
+      __syncwarp();
+      int bb = 0;
+#pragma unroll 1
+      for (int it = lane; it < total; it += 32) {
+        while (it >= incl[bb]) ++bb;
+        const int c = lo_s[bb] + (it - (bb ? incl[bb - 1] : 0));
+        float ar[BS];
+        const float4* r4 = reinterpret_cast<const float4*>(rows + bb * BS);
+#pragma unroll
+        for (int v = 0; v < BS / 4; ++v) {
+          float4 t = r4[v];
+          ar[4 * v] = t.x; ar[4 * v + 1] = t.y; ar[4 * v + 2] = t.z; ar[4 * v + 3] = t.w;
+        }
+        const float E = block_sse<BS, MODE>(ar, cand_value<FMT>(c));
+        atomicMin(best + bb, ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)c);
+      }
+      __syncwarp();
+      const unsigned win = (unsigned)(best[lane] & 0xffffffffu);
+      if (win != 0) s = cand_value<FMT>((int)win);
+      __syncwarp();  // rows/best are rewritten by the next chunk
+    } else if constexpr (METHOD == kTwoArgmin) {
+      if (valid && !s_nan) {
+        int e0 = ue8m0_naive_exp(amax_bits);
+        int e1 = e0 + 1 > 254 ? 254 : e0 + 1;
+        float s1 = pow2f(e1 - 127);
+        if (block_sse_argmin<BS>(x, s1) < block_sse_argmin<BS>(x, s)) s = s1;
+      }
     }
-    write_block<BS, FMT, METHOD, DT>(p, b, x, a, s);
+    if (valid) write_block<BS, FMT, METHOD, DT>(p, blk, x, s);
   }
 }
 
 // Hessian method: CTA (j, row chunk); the CTA's H_j lives in shared memory.
 template <int BS, int FMT, int DT>
 __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
+  constexpr int MODE = Mode<FMT, DT>::v;
   __shared__ __align__(16) float Hs[BS * BS];
   const int64_t j = blockIdx.x;
   const float* Hg = p.h_blocks + j * (BS * BS);
@@ -336,8 +507,8 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
     uint32_t amax_bits = abs_and_amax<BS>(x, a);
     float s = naive_scale<FMT>(amax_bits);
     if (!is_nan_bits(__float_as_uint(s) & 0x7fffffffu)) {
-      float E0 = block_sse<BS, DT>(a, s);
-      float best_E = block_hess<BS, DT>(x, a, s, Hs);
+      float E0 = block_sse<BS, MODE>(a, s);
+      float best_E = block_hess<BS, MODE>(x, a, s, Hs);
       int lo, hi;
       search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
 #pragma unroll 1
@@ -348,17 +519,37 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
         // MXFP4: the baseline SSE (mxfp4/reference.py:346).
         bool pass = FMT == kNVFP4 ? (Hc < __fmul_rn(best_E, 10.0f)) : (Hc < E0);
         if (!pass) continue;
-        float E = block_hess<BS, DT>(x, a, sc, Hs);
+        float E = block_hess<BS, MODE>(x, a, sc, Hs);
         if (E < best_E) { best_E = E; s = sc; }
       }
     }
-    write_block<BS, FMT, kHessian, DT>(p, b, x, a, s);
+    write_block<BS, FMT, kHessian, DT>(p, b, x, s);
   }
 }
 
 // ---------------------------------------------------------------------------
 // host-side launch
 // ---------------------------------------------------------------------------
+template <int BS, int FMT, int METHOD, int DT>
+static cudaError_t launch_q(const QuantArgs& p, int num_sms, cudaStream_t st) {
+  using G = WarpGeom<BS, DT, METHOD>;
+  const int smem = kWarps * G::kBytesAligned;
+  cudaError_t e = cudaFuncSetAttribute(quantize_kernel<BS, FMT, METHOD, DT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &per_sm, quantize_kernel<BS, FMT, METHOD, DT>, kThreads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t n_chunks = (p.n_blocks + 31) / 32;
+  int64_t want = (n_chunks + kWarps - 1) / kWarps;
+  int64_t cap = (int64_t)num_sms * per_sm;
+  unsigned grid = (unsigned)(want < cap ? want : cap);
+  quantize_kernel<BS, FMT, METHOD, DT><<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <int BS, int FMT, int DT>
 static cudaError_t launch_fmt_dt(const QuantArgs& p, int method, int num_sms, cudaStream_t st) {
   if (method == kHessian) {
@@ -373,19 +564,13 @@ static cudaError_t launch_fmt_dt(const QuantArgs& p, int method, int num_sms, cu
     hessian_kernel<BS, FMT, DT><<<grid, 128, 0, st>>>(p);
     return cudaGetLastError();
   }
-  const int threads = 256;
-  int64_t blocks = (p.n_blocks + threads - 1) / threads;
-  int64_t cap = (int64_t)num_sms * 8;
-  unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
-  if (grid == 0) return cudaSuccess;
   switch (method) {
-    case kNaive: quantize_kernel<BS, FMT, kNaive, DT><<<grid, threads, 0, st>>>(p); break;
-    case kSSE: quantize_kernel<BS, FMT, kSSE, DT><<<grid, threads, 0, st>>>(p); break;
-    case kNaiveArgmin: quantize_kernel<BS, FMT, kNaiveArgmin, DT><<<grid, threads, 0, st>>>(p); break;
-    case kTwoArgmin: quantize_kernel<BS, FMT, kTwoArgmin, DT><<<grid, threads, 0, st>>>(p); break;
+    case kNaive: return launch_q<BS, FMT, kNaive, DT>(p, num_sms, st);
+    case kSSE: return launch_q<BS, FMT, kSSE, DT>(p, num_sms, st);
+    case kNaiveArgmin: return launch_q<BS, FMT, kNaiveArgmin, DT>(p, num_sms, st);
+    case kTwoArgmin: return launch_q<BS, FMT, kTwoArgmin, DT>(p, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 template <int BS, int FMT>
@@ -399,11 +584,19 @@ static cudaError_t launch_fmt(const QuantArgs& p, int dtype, int method, int sms
 
 cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int method,
                             int num_sms, cudaStream_t st) {
+  if (p.n_blocks == 0) return cudaSuccess;
   if (bs == 16)
     return fmt == kNVFP4 ? launch_fmt<16, kNVFP4>(p, dtype, method, num_sms, st)
                          : launch_fmt<16, kMXFP4>(p, dtype, method, num_sms, st);
   return fmt == kNVFP4 ? launch_fmt<32, kNVFP4>(p, dtype, method, num_sms, st)
                        : launch_fmt<32, kMXFP4>(p, dtype, method, num_sms, st);
+}
+
+cudaError_t read_device_error_quantize(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, qz_device_error, sizeof(unsigned));
+  if (e != cudaSuccess || !clear) return e;
+  unsigned zero = 0;
+  return cudaMemcpyToSymbol(qz_device_error, &zero, sizeof(unsigned));
 }
 
 }  // namespace qz
