@@ -35,6 +35,15 @@ __device__ __forceinline__ constexpr float cbv(int k) {
        : k == 4 ? 2.0f : k == 5 ? 3.0f : k == 6 ? 4.0f : 6.0f;
 }
 
+// Codebook value of a runtime index 0..7 without a table or branches:
+// for c >= 2 the E2M1 value 2^((c>>1)-1) * (1 + (c&1)/2) has fp32 bits
+// (c << 22) + 0x3f000000; c = 1 is 0.5 and c = 0 is 0.
+__device__ __forceinline__ float cb_rt(uint32_t c) {
+  float v = __uint_as_float((c << 22) + 0x3f000000u);
+  v = c == 1u ? 0.5f : v;
+  return c == 0u ? 0.0f : v;
+}
+
 __device__ __forceinline__ bool is_nan_bits(uint32_t abs_bits) { return abs_bits > 0x7f800000u; }
 
 // x.to(float8_e4m3fn).to(float32) for x >= 0 or NaN: round to nearest even,

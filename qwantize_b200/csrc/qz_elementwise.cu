@@ -32,7 +32,7 @@ __global__ void dequantize_kernel(const float* __restrict__ scales, const float4
 }
 
 __device__ __forceinline__ float e2m1_value(uint32_t nib) {
-  float m = cbv((int)(nib & 7u));
+  float m = cb_rt(nib & 7u);
   return (nib & 8u) ? -m : m;
 }
 

@@ -216,7 +216,12 @@ __device__ __forceinline__ float cand_value(int c) {
 }
 
 // Signed codebook of mxfp4/kernels.py:284-287 (entry 8 is +0.0).
-__device__ __forceinline__ float cb16(int k) { return k < 8 ? cbv(k) : (k == 8 ? 0.0f : -cbv(k - 8)); }
+__device__ __forceinline__ float cb16(int k) {
+  float m = cb_rt((uint32_t)k & 7u);
+  return k < 8 ? m : -m;  // (k = 8 gives -0.0: same deltas as the table's +0.0)
+}
+// The table entry itself, as stored in the output (entry 8 is +0.0).
+__device__ __forceinline__ float cb16_entry(int k) { return k == 8 ? 0.0f : cb16(k); }
 
 // argmin_k |x - s*cb16[k]| with torch.argmin semantics (the first NaN wins,
 // else the first minimum).
@@ -258,11 +263,11 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
   for (int i = 0; i < BS; ++i) {
     if (argmin) {
       int k = argmin_index(x[i], s);
-      quant[i] = cb16(k);
+      quant[i] = cb16_entry(k);
       nib[i] = k < 8 ? k : (k == 8 ? 0 : 8 + (k - 8));
     } else {
       int idx = fp4_index<MODE>(fabsf(x[i]), s);
-      float q = cbv(idx);
+      float q = cb_rt((uint32_t)idx);
       quant[i] = x[i] > 0.0f ? q : (x[i] < 0.0f ? -q : 0.0f);  // torch.sign semantics
       nib[i] = (x[i] < 0.0f ? 8u : 0u) | ((x[i] > 0.0f || x[i] < 0.0f) ? (uint32_t)idx : 0u);
     }
@@ -359,11 +364,11 @@ __device__ __forceinline__ void smem_block(const unsigned char* raw, float (&x)[
 constexpr int kWarps = 8;             // warps per CTA
 constexpr int kThreads = kWarps * 32;
 
-template <int BS, int DT, int METHOD>
+template <int BS, int FMT, int DT, int METHOD>
 struct WarpGeom {
   static constexpr int kChunkBytes = 32 * BS * Elem<DT>::kSize;  // 1-4 KB
   static constexpr int kStages = kChunkBytes <= 2048 ? 4 : 2;
-  static constexpr bool kCoop = METHOD == kSSE;
+  static constexpr bool kCoop = METHOD == kSSE && FMT == kNVFP4;
   static constexpr int kRowBytes = kCoop ? 32 * BS * 4 : 0;     // |x| rows for cooperation
   static constexpr int kBytes = kStages * kChunkBytes + kRowBytes + (kCoop ? 32 * 8 + 64 * 4 : 0) +
                                 kStages * 8;
@@ -373,7 +378,7 @@ struct WarpGeom {
 // Naive / SSE / argmin methods.
 template <int BS, int FMT, int METHOD, int DT>
 __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
-  using G = WarpGeom<BS, DT, METHOD>;
+  using G = WarpGeom<BS, FMT, DT, METHOD>;
   constexpr int MODE = Mode<FMT, DT>::v;
   constexpr int S = G::kStages;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -434,7 +439,22 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
     float s = naive_scale<FMT>(amax_bits);
     const bool s_nan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
 
-    if constexpr (METHOD == kSSE) {
+    if constexpr (METHOD == kSSE && !G::kCoop) {
+      // MXFP4: 1-4 power-of-two candidates per block; each lane walks its own
+      // (the ascending loop with strict '<', clipping fast-fail omitted as above).
+      if (valid && !s_nan) {
+        const float E0 = block_sse<BS, MODE>(a, s);
+        int lo, hi;
+        search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
+        float best_E = E0;
+#pragma unroll 1
+        for (int c = lo; c <= hi; ++c) {
+          const float sc = cand_value<FMT>(c);
+          const float E = block_sse<BS, MODE>(a, sc);
+          if (E < best_E) { best_E = E; s = sc; }
+        }
+      }
+    } else if constexpr (METHOD == kSSE) {
       // A NaN naive scale (NaN amax, or NVFP4 amax/6 > 464) makes the
       // reference's E0 and bounds NaN: no candidate is ever in range.
       int lo = 1, hi = 0;
@@ -532,7 +552,7 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
 // ---------------------------------------------------------------------------
 template <int BS, int FMT, int METHOD, int DT>
 static cudaError_t launch_q(const QuantArgs& p, int num_sms, cudaStream_t st) {
-  using G = WarpGeom<BS, DT, METHOD>;
+  using G = WarpGeom<BS, FMT, DT, METHOD>;
   const int smem = kWarps * G::kBytesAligned;
   cudaError_t e = cudaFuncSetAttribute(quantize_kernel<BS, FMT, METHOD, DT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
