@@ -44,6 +44,31 @@ __device__ __forceinline__ float cb_rt(uint32_t c) {
   return c == 0u ? 0.0f : v;
 }
 
+// Hardware E2M1 rounding (sm_100a).  For an input with at most 11 significant
+// bits (bf16 / fp16) and any E4M3 or UE8M0 scale s > 0, rounding
+// y' = |x| * RN(RN(1/s) * (1 - 2^-13)) to nearest-even never meets a tie and
+// equals the reference's bucketize(|x| / s) (ties to the smaller entry):
+// proved exhaustively over all such inputs and scales by
+// tests/test_rounding_cpu.py.  Inf saturates to the largest code.
+constexpr float kBiasDown = 0.9998779296875f;  // 1 - 2^-13
+
+// Two magnitude codes in one byte: lo -> bits 0..3, hi -> bits 4..7.
+__device__ __forceinline__ uint32_t e2m1x2_rn(float lo, float hi) {
+  uint32_t out;
+  asm("{\n .reg .b8 b;\n cvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n cvt.u32.u8 %0, b;\n}\n"
+      : "=r"(out)
+      : "f"(hi), "f"(lo));
+  return out;
+}
+
+// Decode a byte of two (signed) E2M1 codes to fp32 values (exact).
+__device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
+  uint32_t h2;
+  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}\n" : "=r"(h2) : "r"(byte));
+  __half2 h = *reinterpret_cast<__half2*>(&h2);
+  return __half22float2(h);
+}
+
 __device__ __forceinline__ bool is_nan_bits(uint32_t abs_bits) { return abs_bits > 0x7f800000u; }
 
 // x.to(float8_e4m3fn).to(float32) for x >= 0 or NaN: round to nearest even,

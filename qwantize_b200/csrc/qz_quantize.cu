@@ -96,6 +96,29 @@ __device__ __forceinline__ float block_sse(const float (&a)[BS], float s) {
   return sum8<BS>(d2);
 }
 
+// Block SSE with hardware rounding: bf16/fp16 inputs, finite s > 0.
+template <int BS>
+__device__ __forceinline__ float block_sse_hw(const float (&a)[BS], float s) {
+  const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
+  float d2[BS];
+#pragma unroll
+  for (int i = 0; i < BS; i += 2) {
+    const float2 q = e2m1x2_to_float2(e2m1x2_rn(__fmul_rn(a[i], c), __fmul_rn(a[i + 1], c)));
+    const float d0 = __fsub_rn(a[i], __fmul_rn(q.x, s));
+    const float d1 = __fsub_rn(a[i + 1], __fmul_rn(q.y, s));
+    d2[i] = __fmul_rn(d0, d0);
+    d2[i + 1] = __fmul_rn(d1, d1);
+  }
+  return sum8<BS>(d2);
+}
+
+// Candidate SSE: the hardware path for 16-bit inputs, IEEE division for fp32.
+template <int BS, int MODE, int DT>
+__device__ __forceinline__ float cand_sse(const float (&a)[BS], float s) {
+  if constexpr (DT != kDtF32) return block_sse_hw<BS>(a, s);
+  else return block_sse<BS, MODE>(a, s);
+}
+
 // Clipping error sum(clamp(|x| - 6 s, 0)^2) (nvfp4/reference.py:209).
 template <int BS>
 __device__ __forceinline__ float block_clip(const float (&a)[BS], float s) {
@@ -259,6 +282,24 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
   float quant[BS];
   uint32_t nib[BS];
   const bool argmin = METHOD == kNaiveArgmin || METHOD == kTwoArgmin;
+  const uint32_t sb = __float_as_uint(s);
+  // hardware rounding: 16-bit input, finite s > 0, no NaN element (a NaN
+  // element makes amax, hence s, NaN)
+  if (!argmin && DT != kDtF32 && sb > 0u && sb < 0x7f800000u) {
+    const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
+#pragma unroll
+    for (int i = 0; i < BS; i += 2) {
+      uint32_t byte = e2m1x2_rn(__fmul_rn(fabsf(x[i]), c), __fmul_rn(fabsf(x[i + 1]), c));
+      // sign bit for x < 0 only (-0.0 quantizes to +0.0 in the reference)
+      byte |= (__float_as_uint(x[i]) > 0x80000000u ? 0x08u : 0u) |
+              (__float_as_uint(x[i + 1]) > 0x80000000u ? 0x80u : 0u);
+      nib[i] = byte & 0xfu;
+      nib[i + 1] = byte >> 4;
+      const float2 q = e2m1x2_to_float2(byte);
+      quant[i] = q.x;
+      quant[i + 1] = q.y;
+    }
+  } else {
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
     if (argmin) {
@@ -271,6 +312,7 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
       quant[i] = x[i] > 0.0f ? q : (x[i] < 0.0f ? -q : 0.0f);  // torch.sign semantics
       nib[i] = (x[i] < 0.0f ? 8u : 0u) | ((x[i] > 0.0f || x[i] < 0.0f) ? (uint32_t)idx : 0u);
     }
+  }
   }
   const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
   if (p.scales) p.scales[b] = s;
@@ -450,7 +492,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
 #pragma unroll 1
         for (int c = lo; c <= hi; ++c) {
           const float sc = cand_value<FMT>(c);
-          const float E = block_sse<BS, MODE>(a, sc);
+          const float E = cand_sse<BS, MODE, DT>(a, sc);
           if (E < best_E) { best_E = E; s = sc; }
         }
       }
@@ -490,7 +532,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
           float4 t = r4[v];
           ar[4 * v] = t.x; ar[4 * v + 1] = t.y; ar[4 * v + 2] = t.z; ar[4 * v + 3] = t.w;
         }
-        const float E = block_sse<BS, MODE>(ar, cand_value<FMT>(c));
+        const float E = cand_sse<BS, MODE, DT>(ar, cand_value<FMT>(c));
         atomicMin(best + bb, ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)c);
       }
       __syncwarp();
