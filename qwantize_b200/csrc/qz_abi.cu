@@ -57,8 +57,10 @@ const char* qz_last_error(void) { return g_last_error.c_str(); }
 int qz_version(void) { return 100; }
 
 int qz_poll_device_error(int clear, unsigned* flags_out) {
-  unsigned f = 0;
+  unsigned f = 0, g = 0;
   int st = cuda_status(read_device_error_quantize(&f, clear != 0), "qz_poll_device_error");
+  if (st == QZ_OK) st = cuda_status(read_device_error_gemm(&g, clear != 0), "qz_poll_device_error");
+  f |= g;
   if (flags_out) *flags_out = f;
   if (st != QZ_OK) return st;
   if (f) return fail(QZ_ERR_TIMEOUT, "a device-side wait gave up (flags 0x%x)", f);

@@ -1,14 +1,474 @@
-// qz_gemm.cu -- tcgen05 Gram and output-error GEMMs (placeholder entry points
-// until the tensor-core kernels land: they report QZ_ERR_UNSUPPORTED).
+// qz_gemm.cu -- the two dense contractions of the path on the 5th-generation
+// tensor cores (tcgen05 + TMEM + TMA), bf16 operands, fp32 accumulation:
+//
+//   Gram      H = X^T X for X (T, K) row-major (the Hessian build of
+//             nvfp4/reference.py:304-317).  Both operands are column panels of
+//             X read straight from its row-major layout as MN-major tiles (no
+//             transpose pass).  Only tiles touching the upper triangle are
+//             computed; the epilogue writes each (i, j >= i) and its mirror, so
+//             H is exactly symmetric.  The block-diagonal mode runs only the
+//             tiles on the diagonal and writes (K/bs, bs, bs).
+//   Metrics   sum((X W_dq^T - X W^T)^2) and sum((X W^T)^2) (metrics.py:29-50):
+//             one GEMM of X against [W_tile; W_dq_tile] (N = 128 + 128), the
+//             squared-difference reduction done from TMEM in the epilogue, the
+//             T x M products never written.
+//
+// Kernel structure (one persistent CTA per SM, 192 threads):
+//   warp 0   TMA producer: a 4-stage ring of 48 KB operand stages
+//   warp 1   TMEM allocator + MMA issuer (one thread issues tcgen05.mma,
+//            tcgen05.commit frees a smem stage / publishes an accumulator)
+//   warps 2-5 epilogue: tcgen05.ld of the 128 x 256 fp32 accumulator
+//   Two accumulators (2 x 256 TMEM columns) let the epilogue of one tile overlap
+//   the main loop of the next.  Every mbarrier wait is bounded (2 s): on timeout
+//   the kernel records an error flag, all roles stop, TMEM is freed, and the
+//   host reports QZ_ERR_TIMEOUT.  No TMA multicast anywhere.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
 #include "../../include/qwantize_b200.h"
 #include "qz_kernels.h"
+#include "qz_ptx.cuh"
 
-namespace qz { int fail(int code, const char* fmt, ...); }
+namespace qz {
 
-extern "C" int qz_gram(const uint16_t*, int64_t, int64_t, int, int, int, float*, void*) {
-  return qz::fail(QZ_ERR_UNSUPPORTED, "qz_gram: not built yet");
+int fail(int code, const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+int current_sms(int* sms);
+
+constexpr int kGemmThreads = 192;
+constexpr int kStages = 4;
+constexpr int kBM = 128, kBN = 256, kBK = 64;     // tile M x N x K-step
+constexpr int kStageBytes = (kBM + kBN) * kBK * 2;  // 48 KB
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2 };
+
+struct GemmParams {
+  int64_t T, K, M;      // Gram: X is (T, K); Metrics: X (T, K), W (M, K)
+  int bs;               // block size for kGramDiag
+  int accumulate;
+  int64_t tiles_m, tiles_n, n_tiles;
+  float* H;
+  double* sums;
+  uint32_t lbo, sbo;    // MN-major descriptor offsets (bytes)
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers specific to the tensor-core pipeline
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
-extern "C" int qz_output_error_sums(const uint16_t*, int64_t, int64_t, const uint16_t*,
-                                    const uint16_t*, int64_t, double*, void*) {
-  return qz::fail(QZ_ERR_UNSUPPORTED, "qz_output_error_sums: not built yet");
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 inputs, fp32 accumulate).
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 bits, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (tcgen05), 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fffu);
+  d |= (uint64_t)((lbo >> 4) & 0x3fffu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3fffu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16: bf16 x bf16 -> fp32, M x N.
+__host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                       // D format: f32
+         | (1u << 7)                     // A format: bf16
+         | (1u << 10)                    // B format: bf16
+         | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// tile enumeration
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64_t t, int64_t& mi, int64_t& nj) {
+  if (mode == kGramDiag) {
+    mi = t;
+    nj = (t * kBM) / kBN;
+    return;
+  }
+  if (mode == kMetrics) {
+    mi = t / p.tiles_n;
+    nj = t % p.tiles_n;
+    return;
+  }
+  // kGramFull: rows mi = 0.., in each row the n-tiles with nj*256 + 255 >= mi*128
+  // (the first is (mi*128)/256); rows are enumerated in order.
+  int64_t r = t;
+  int64_t row = 0;
+  while (true) {
+    int64_t first = (row * kBM) / kBN;
+    int64_t cnt = p.tiles_n - first;
+    if (r < cnt) { mi = row; nj = first + r; return; }
+    r -= cnt;
+    ++row;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_c, GemmParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_base_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t k_steps = (MODE == kMetrics ? (p.K + kBK - 1) / kBK : (p.T + kBK - 1) / kBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 128); }
+    *abort_s = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_base_s, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_s;
+
+  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned err) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+      if (*abort_s) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(&qz_device_error, err);
+        *abort_s = 1;
+        return false;
+      }
+    }
+    return true;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x) {
+        int64_t mi, nj;
+        tile_coords(p, MODE, t, mi, nj);
+        for (int64_t ks = 0; ks < k_steps; ++ks, ++it) {
+          const int s = it % kStages;
+          if (!wait(empty + s, ((it / kStages) & 1) ^ 1, kDevErrLoadTimeout)) goto producer_done;
+          unsigned char* sa = smem + s * kStageBytes;
+          unsigned char* sb = sa + kBM * kBK * 2;
+          mbar_arrive_expect_tx(full + s, kStageBytes);
+          if (MODE == kMetrics) {
+            const int kx = (int)(ks * kBK);
+            tma_load_2d(sa, &map_a, kx, (int)(mi * kBM), full + s);                // X rows (t)
+            tma_load_2d(sb, &map_b, kx, (int)(nj * 128), full + s);                // W rows
+            tma_load_2d(sb + 128 * kBK * 2, &map_c, kx, (int)(nj * 128), full + s); // W_dq rows
+          } else {
+            const int ty = (int)(ks * kBK);
+            const int i0 = (int)(mi * kBM), j0 = (int)(nj * kBN);
+            tma_load_2d(sa, &map_a, i0, ty, full + s);
+            tma_load_2d(sa + 8192, &map_a, i0 + 64, ty, full + s);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tma_load_2d(sb + 8192 * q, &map_a, j0 + 64 * q, ty, full + s);
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr bool mn = MODE != kMetrics;
+      constexpr uint32_t idesc = instr_desc(kBM, kBN, mn, mn);
+      uint32_t it = 0, lt = 0;
+      for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
+        const uint32_t acc = lt & 1;
+        if (!wait(tempty + acc, ((lt >> 1) & 1) ^ 1, kDevErrMmaTimeout)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        bool ok = true;
+        for (int64_t ks = 0; ks < k_steps; ++ks, ++it) {
+          const int s = it % kStages;
+          if (!wait(full + s, (it / kStages) & 1, kDevErrMmaTimeout)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kBM * kBK * 2;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            uint64_t ad, bd;
+            if (mn) {  // MN-major: a 16-row K step is two 8-row swizzle atoms (2 KB)
+              ad = smem_desc(sa + kk * 2048, p.lbo, p.sbo);
+              bd = smem_desc(sb + kk * 2048, p.lbo, p.sbo);
+            } else {   // K-major: 16 elements = 32 bytes inside the 128-byte swizzle row
+              ad = smem_desc(sa + kk * 32, 16, 1024);
+              bd = smem_desc(sb + kk * 32, 16, 1024);
+            }
+            umma_bf16(d_tmem, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(empty + s);
+        }
+        if (!ok) break;
+        umma_commit(tfull + acc);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31
+    const int row = quarter * 32 + lane;     // accumulator row of this thread
+    uint32_t lt = 0;
+    double part0 = 0.0, part1 = 0.0;
+    for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
+      int64_t mi, nj;
+      tile_coords(p, MODE, t, mi, nj);
+      const uint32_t acc = lt & 1;
+      if (!wait(tfull + acc, (lt >> 1) & 1, kDevErrEpilogueTimeout)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN;
+      if (MODE == kMetrics) {
+        const int64_t trow = mi * kBM + row;
+        float e = 0.0f, r2 = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 16) {
+          float ref[16], dq[16];
+          tmem_ld16(taddr + c, ref);
+          tmem_ld16(taddr + 128 + c, dq);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float d = dq[q] - ref[q];
+            e = fmaf(d, d, e);
+            r2 = fmaf(ref[q], ref[q], r2);
+          }
+        }
+        if (trow < p.T) { part0 += (double)e; part1 += (double)r2; }
+      } else {
+        const int64_t i = mi * kBM + row;
+        const int64_t j0 = nj * kBN;
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          if (i >= p.K) continue;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int64_t j = j0 + c + q;
+            if (j >= p.K) continue;
+            if (MODE == kGramFull) {
+              if (j < i) continue;
+              float* up = p.H + i * p.K + j;
+              float* lo = p.H + j * p.K + i;
+              const float val = p.accumulate ? v[q] + *up : v[q];
+              *up = val;
+              if (j > i) *lo = val;
+            } else {
+              if (j / p.bs != i / p.bs) continue;
+              float* h = p.H + (i / p.bs) * p.bs * p.bs + (i % p.bs) * p.bs + (j % p.bs);
+              *h = p.accumulate ? *h + v[q] : v[q];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty + acc);
+    }
+    if (MODE == kMetrics) {
+      // warp reduce, one atomic pair per warp
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        part0 += __shfl_xor_sync(0xffffffffu, part0, o);
+        part1 += __shfl_xor_sync(0xffffffffu, part1, o);
+      }
+      if (lane == 0) {
+        atomicAdd(p.sums, part0);
+        atomicAdd(p.sums + 1, part1);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map: rows of `inner` elements, `outer` rows, box inner x outer.
+static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                    uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(QZ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QZ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QZ_OK;
+}
+
+template <int MODE>
+static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, GemmParams p,
+                       cudaStream_t st) {
+  int sms = 0;
+  int s = current_sms(&sms);
+  if (s != QZ_OK) return s;
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute");
+  const int64_t grid = p.n_tiles < sms ? p.n_tiles : sms;
+  if (grid <= 0) return QZ_OK;
+  gemm_kernel<MODE><<<(unsigned)grid, kGemmThreads, kSmemBytes, st>>>(a, b, c, p);
+  return cuda_status(cudaGetLastError(), "gemm launch");
+}
+
+// MN-major descriptor offsets; overridable for validation (QZ_MN_LBO / QZ_MN_SBO).
+static void mn_offsets(uint32_t* lbo, uint32_t* sbo) {
+  *lbo = 8192;  // between 64-element swizzle atoms along M / N
+  *sbo = 1024;  // between 8-row groups along K
+  if (const char* v = getenv("QZ_MN_LBO")) *lbo = (uint32_t)atoi(v);
+  if (const char* v = getenv("QZ_MN_SBO")) *sbo = (uint32_t)atoi(v);
+}
+
+cudaError_t read_device_error_gemm(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, qz_device_error, sizeof(unsigned));
+  if (e != cudaSuccess || !clear) return e;
+  unsigned zero = 0;
+  return cudaMemcpyToSymbol(qz_device_error, &zero, sizeof(unsigned));
+}
+
+}  // namespace qz
+
+using namespace qz;
+
+extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int block_size, int accumulate,
+                       float* H, void* stream) {
+  if (mode != QZ_GRAM_FULL && mode != QZ_GRAM_BLOCKDIAG) return fail(QZ_ERR_INVALID, "unknown gram mode %d", mode);
+  if (T < 0 || K <= 0) return fail(QZ_ERR_INVALID, "need T >= 0 and K > 0");
+  if (K % 8 != 0) return fail(QZ_ERR_INVALID, "K must be a multiple of 8 (16-byte rows for TMA)");
+  if (mode == QZ_GRAM_BLOCKDIAG && ((block_size != 16 && block_size != 32) || K % block_size != 0))
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32 and divide K");
+  if (K > 2147483647LL || T > 2147483647LL) return fail(QZ_ERR_INVALID, "T and K must fit in int32");
+  if (!H) return fail(QZ_ERR_INVALID, "H is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n_out = mode == QZ_GRAM_FULL ? K * K : K * block_size;
+  if (T == 0) {
+    if (accumulate) return QZ_OK;
+    return cuda_status(cudaMemsetAsync(H, 0, (size_t)n_out * 4, st), "cudaMemsetAsync");
+  }
+  if (!X) return fail(QZ_ERR_INVALID, "X is NULL");
+  if (reinterpret_cast<uintptr_t>(X) % 16) return fail(QZ_ERR_INVALID, "X must be 16-byte aligned");
+  CUtensorMap map;
+  int s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
+  if (s != QZ_OK) return s;
+  GemmParams p{};
+  p.T = T; p.K = K; p.M = 0; p.bs = block_size; p.accumulate = accumulate; p.H = H;
+  mn_offsets(&p.lbo, &p.sbo);
+  p.tiles_m = (K + kBM - 1) / kBM;
+  p.tiles_n = (K + kBN - 1) / kBN;
+  if (mode == QZ_GRAM_FULL) {
+    int64_t n = 0;
+    for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / kBN;
+    p.n_tiles = n;
+    return launch_gemm<kGramFull>(map, map, map, p, st);
+  }
+  p.n_tiles = p.tiles_m;
+  return launch_gemm<kGramDiag>(map, map, map, p, st);
+}
+
+extern "C" int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, const uint16_t* W,
+                                    const uint16_t* W_dq, int64_t M, double* sums, void* stream) {
+  if (T < 0 || K <= 0 || M <= 0) return fail(QZ_ERR_INVALID, "need T >= 0, K > 0, M > 0");
+  if (K % 8 != 0) return fail(QZ_ERR_INVALID, "K must be a multiple of 8 (16-byte rows for TMA)");
+  if (K > 2147483647LL || T > 2147483647LL || M > 2147483647LL)
+    return fail(QZ_ERR_INVALID, "T, K and M must fit in int32");
+  if (!X || !W || !W_dq || !sums) return fail(QZ_ERR_INVALID, "NULL pointer");
+  if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(W_dq)) % 16)
+    return fail(QZ_ERR_INVALID, "X, W and W_dq must be 16-byte aligned");
+  if (T == 0) return QZ_OK;
+  CUtensorMap mx, mw, mq;
+  int s = make_map(&mx, X, (uint64_t)K, (uint64_t)T, 64, 128);
+  if (s == QZ_OK) s = make_map(&mw, W, (uint64_t)K, (uint64_t)M, 64, 128);
+  if (s == QZ_OK) s = make_map(&mq, W_dq, (uint64_t)K, (uint64_t)M, 64, 128);
+  if (s != QZ_OK) return s;
+  GemmParams p{};
+  p.T = T; p.K = K; p.M = M; p.sums = sums;
+  p.tiles_m = (T + kBM - 1) / kBM;
+  p.tiles_n = (M + 127) / 128;
+  p.n_tiles = p.tiles_m * p.tiles_n;
+  return launch_gemm<kMetrics>(mx, mw, mq, p, static_cast<cudaStream_t>(stream));
 }
