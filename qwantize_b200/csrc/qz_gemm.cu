@@ -39,19 +39,33 @@ int cuda_status(cudaError_t e, const char* what);
 int current_sms(int* sms);
 
 constexpr int kGemmThreads = 192;
-constexpr int kStages = 4;
-constexpr int kBM = 128, kBN = 256, kBK = 64;     // tile M x N x K-step
-constexpr int kStageBytes = (kBM + kBN) * kBK * 2;  // 48 KB
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kBM = 128, kBK = 64;  // tile rows, K-step (64 bf16 = one 128-byte swizzle row)
 
 enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2 };
+
+// Per-mode geometry.  Full Gram / metrics: 128 x 256 tiles, A 16 KB + B 32 KB
+// per stage, 4 stages, two 256-column accumulators (all 512 TMEM columns).
+// Block-diagonal Gram: 128 x 128 diagonal tiles whose A and B panels are the
+// same columns of X, so one 16 KB panel per stage feeds both operands; 8 stages.
+template <int MODE>
+struct Geo {
+  static constexpr int BN = MODE == kGramDiag ? 128 : 256;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = MODE == kGramDiag ? 0 : BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = MODE == kGramDiag ? 8 : 4;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
 
 struct GemmParams {
   int64_t T, K, M;      // Gram: X is (T, K); Metrics: X (T, K), W (M, K)
   int bs;               // block size for kGramDiag
-  int accumulate;
+  int accumulate;       // add into H instead of storing
   int64_t tiles_m, tiles_n, n_tiles;
+  int64_t splits, split_rows;  // kGramDiag: T is cut into `splits` ranges of split_rows
   float* H;
+  float* partials;      // kGramDiag: splits-1 partial (K/bs, bs, bs) buffers
   double* sums;
   uint32_t lbo, sbo;    // MN-major descriptor offsets (bytes)
 };
@@ -133,9 +147,9 @@ __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool a_mn_major,
 // tile enumeration
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64_t t, int64_t& mi, int64_t& nj) {
-  if (mode == kGramDiag) {
-    mi = t;
-    nj = (t * kBM) / kBN;
+  if (mode == kGramDiag) {  // unit t = (split, tile): tile = t % tiles_m
+    mi = t % p.tiles_m;
+    nj = t / p.tiles_m;     // the split index
     return;
   }
   if (mode == kMetrics) {
@@ -148,7 +162,7 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64
   int64_t r = t;
   int64_t row = 0;
   while (true) {
-    int64_t first = (row * kBM) / kBN;
+    int64_t first = (row * kBM) / 256;
     int64_t cnt = p.tiles_n - first;
     if (r < cnt) { mi = row; nj = first + r; return; }
     r -= cnt;
@@ -159,29 +173,40 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// Rows [r0, r1) of X that unit t reduces over (Gram), or K-steps (metrics).
+template <int MODE>
+__device__ __forceinline__ int64_t unit_steps(const GemmParams& p, int64_t nj, int64_t& r0) {
+  if (MODE == kMetrics) { r0 = 0; return (p.K + kBK - 1) / kBK; }
+  if (MODE == kGramFull) { r0 = 0; return (p.T + kBK - 1) / kBK; }
+  r0 = nj * p.split_rows;
+  int64_t r1 = r0 + p.split_rows < p.T ? r0 + p.split_rows : p.T;
+  return (r1 - r0 + kBK - 1) / kBK;
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_c, GemmParams p) {
+  using G = Geo<MODE>;
+  constexpr int BN = G::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kStageBytes);
+  uint64_t* empty = full + G::kStages;
+  uint64_t* tfull = empty + G::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_base_s + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t k_steps = (MODE == kMetrics ? (p.K + kBK - 1) / kBK : (p.T + kBK - 1) / kBK);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int s = 0; s < G::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 128); }
     *abort_s = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_base_s, 512);
+  if (warp == 1) tmem_alloc(tmem_base_s, G::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -206,26 +231,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x) {
-        int64_t mi, nj;
+        int64_t mi, nj, r0;
         tile_coords(p, MODE, t, mi, nj);
+        const int64_t k_steps = unit_steps<MODE>(p, nj, r0);
         for (int64_t ks = 0; ks < k_steps; ++ks, ++it) {
-          const int s = it % kStages;
-          if (!wait(empty + s, ((it / kStages) & 1) ^ 1, kDevErrLoadTimeout)) goto producer_done;
-          unsigned char* sa = smem + s * kStageBytes;
-          unsigned char* sb = sa + kBM * kBK * 2;
-          mbar_arrive_expect_tx(full + s, kStageBytes);
+          const int s = it % G::kStages;
+          if (!wait(empty + s, ((it / G::kStages) & 1) ^ 1, kDevErrLoadTimeout)) goto producer_done;
+          unsigned char* sa = smem + s * G::kStageBytes;
+          unsigned char* sb = sa + G::kABytes;
+          mbar_arrive_expect_tx(full + s, G::kStageBytes);
           if (MODE == kMetrics) {
             const int kx = (int)(ks * kBK);
-            tma_load_2d(sa, &map_a, kx, (int)(mi * kBM), full + s);                // X rows (t)
-            tma_load_2d(sb, &map_b, kx, (int)(nj * 128), full + s);                // W rows
-            tma_load_2d(sb + 128 * kBK * 2, &map_c, kx, (int)(nj * 128), full + s); // W_dq rows
+            tma_load_2d(sa, &map_a, kx, (int)(mi * kBM), full + s);                 // X rows (t)
+            tma_load_2d(sb, &map_b, kx, (int)(nj * 128), full + s);                 // W rows
+            tma_load_2d(sb + 128 * kBK * 2, &map_c, kx, (int)(nj * 128), full + s);  // W_dq rows
           } else {
-            const int ty = (int)(ks * kBK);
-            const int i0 = (int)(mi * kBM), j0 = (int)(nj * kBN);
+            const int ty = (int)(r0 + ks * kBK);
+            const int i0 = (int)(mi * kBM);
             tma_load_2d(sa, &map_a, i0, ty, full + s);
             tma_load_2d(sa + 8192, &map_a, i0 + 64, ty, full + s);
+            if (MODE == kGramFull) {
+              const int j0 = (int)(nj * BN);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) tma_load_2d(sb + 8192 * q, &map_a, j0 + 64 * q, ty, full + s);
+              for (int q = 0; q < 4; ++q) tma_load_2d(sb + 8192 * q, &map_a, j0 + 64 * q, ty, full + s);
+            }
           }
         }
       }
@@ -235,20 +264,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr bool mn = MODE != kMetrics;
-      constexpr uint32_t idesc = instr_desc(kBM, kBN, mn, mn);
+      constexpr uint32_t idesc = instr_desc(kBM, BN, mn, mn);
       uint32_t it = 0, lt = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
+        int64_t mi, nj, r0;
+        tile_coords(p, MODE, t, mi, nj);
+        const int64_t k_steps = unit_steps<MODE>(p, nj, r0);
         const uint32_t acc = lt & 1;
         if (!wait(tempty + acc, ((lt >> 1) & 1) ^ 1, kDevErrMmaTimeout)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kBN;
+        const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int64_t ks = 0; ks < k_steps; ++ks, ++it) {
-          const int s = it % kStages;
-          if (!wait(full + s, (it / kStages) & 1, kDevErrMmaTimeout)) { ok = false; break; }
+          const int s = it % G::kStages;
+          if (!wait(full + s, (it / G::kStages) & 1, kDevErrMmaTimeout)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * kStageBytes);
-          const uint32_t sb = sa + kBM * kBK * 2;
+          const uint32_t sa = smem_u32(smem + s * G::kStageBytes);
+          const uint32_t sb = MODE == kGramDiag ? sa : sa + G::kABytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             uint64_t ad, bd;
@@ -279,7 +311,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t acc = lt & 1;
       if (!wait(tfull + acc, (lt >> 1) & 1, kDevErrEpilogueTimeout)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kBN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (MODE == kMetrics) {
         const int64_t trow = mi * kBM + row;
         float e = 0.0f, r2 = 0.0f;
@@ -296,29 +328,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (trow < p.T) { part0 += (double)e; part1 += (double)r2; }
+      } else if (MODE == kGramDiag) {
+        // this warp's rows 32q..32q+31 meet the diagonal in columns 32q..32q+31
+        float v[32];
+        float* v0 = v;
+        tmem_ld16(taddr + quarter * 32, *reinterpret_cast<float(*)[16]>(v0));
+        tmem_ld16(taddr + quarter * 32 + 16, *reinterpret_cast<float(*)[16]>(v0 + 16));
+        const int64_t i = mi * kBM + row;
+        if (i < p.K) {
+          const int bs = p.bs;
+          const bool hi = bs == 16 && lane >= 16;  // bs 16: the second 16-column block
+          float* dst = (nj == 0 ? p.H : p.partials + (nj - 1) * p.K * bs) + (i / bs) * bs * bs + (i % bs) * bs;
+          const bool add = nj == 0 && p.accumulate;
+#pragma unroll
+          for (int q = 0; q < 32; q += 4) {
+            if (q >= bs) break;
+            float4 w = hi ? make_float4(v[16 + (q & 15)], v[17 + (q & 15)], v[18 + (q & 15)], v[19 + (q & 15)])
+                          : make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+            float4* d4 = reinterpret_cast<float4*>(dst + q);
+            if (add) {
+              float4 o = *d4;
+              w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+            }
+            *d4 = w;
+          }
+        }
       } else {
         const int64_t i = mi * kBM + row;
-        const int64_t j0 = nj * kBN;
+        const int64_t j0 = nj * BN;
 #pragma unroll 1
-        for (int c = 0; c < kBN; c += 16) {
+        for (int c = 0; c < BN; c += 16) {
           float v[16];
           tmem_ld16(taddr + c, v);
           if (i >= p.K) continue;
+          const int64_t jc = j0 + c;
+          if (jc >= i + 1 && jc + 16 <= p.K) {
+            // whole chunk strictly right of the diagonal: vector row stores
+            float4* up = reinterpret_cast<float4*>(p.H + i * p.K + jc);
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const int64_t j = j0 + c + q;
-            if (j >= p.K) continue;
-            if (MODE == kGramFull) {
-              if (j < i) continue;
+            for (int q = 0; q < 4; ++q) {
+              float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              if (p.accumulate) {
+                float4 o = up[q];
+                w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+              }
+              up[q] = w;
+              v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) p.H[(jc + q) * p.K + i] = v[q];  // mirror: coalesced over lanes
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const int64_t j = jc + q;
+              if (j >= p.K || j < i) continue;
               float* up = p.H + i * p.K + j;
-              float* lo = p.H + j * p.K + i;
               const float val = p.accumulate ? v[q] + *up : v[q];
               *up = val;
-              if (j > i) *lo = val;
-            } else {
-              if (j / p.bs != i / p.bs) continue;
-              float* h = p.H + (i / p.bs) * p.bs * p.bs + (i % p.bs) * p.bs + (j % p.bs);
-              *h = p.accumulate ? *h + v[q] : v[q];
+              if (j > i) p.H[j * p.K + i] = val;
             }
           }
         }
@@ -343,7 +410,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, G::kTmemCols);
+  }
+}
+
+// H += partials[0] + partials[1] + ... in a fixed order (deterministic).
+__global__ void add_partials_kernel(float4* __restrict__ H, const float4* __restrict__ parts, int64_t n4,
+                                    int64_t n_parts) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 h = H[i];
+    for (int64_t k = 0; k < n_parts; ++k) {
+      float4 q = parts[k * n4 + i];
+      h.x += q.x; h.y += q.y; h.z += q.z; h.w += q.w;
+    }
+    H[i] = h;
   }
 }
 
@@ -388,12 +469,21 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   int sms = 0;
   int s = current_sms(&sms);
   if (s != QZ_OK) return s;
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<MODE>::kSmem);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute");
   const int64_t grid = p.n_tiles < sms ? p.n_tiles : sms;
   if (grid <= 0) return QZ_OK;
-  gemm_kernel<MODE><<<(unsigned)grid, kGemmThreads, kSmemBytes, st>>>(a, b, c, p);
+  gemm_kernel<MODE><<<(unsigned)grid, kGemmThreads, Geo<MODE>::kSmem, st>>>(a, b, c, p);
   return cuda_status(cudaGetLastError(), "gemm launch");
+}
+
+
+// Token rows per full-Gram launch (QZ_GRAM_SEGMENT overrides; a multiple of 64).
+static int64_t gram_segment_rows() {
+  int64_t seg = 65536;
+  if (const char* v = getenv("QZ_GRAM_SEGMENT")) seg = atoll(v);
+  if (seg < 64) seg = 64;
+  return seg / 64 * 64;
 }
 
 // MN-major descriptor offsets; overridable for validation (QZ_MN_LBO / QZ_MN_SBO).
@@ -432,22 +522,67 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   }
   if (!X) return fail(QZ_ERR_INVALID, "X is NULL");
   if (reinterpret_cast<uintptr_t>(X) % 16) return fail(QZ_ERR_INVALID, "X must be 16-byte aligned");
-  CUtensorMap map;
-  int s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
-  if (s != QZ_OK) return s;
   GemmParams p{};
-  p.T = T; p.K = K; p.M = 0; p.bs = block_size; p.accumulate = accumulate; p.H = H;
+  p.K = K; p.M = 0; p.bs = block_size; p.H = H;
   mn_offsets(&p.lbo, &p.sbo);
   p.tiles_m = (K + kBM - 1) / kBM;
-  p.tiles_n = (K + kBN - 1) / kBN;
+  int sms = 0;
+  int s = current_sms(&sms);
+  if (s != QZ_OK) return s;
   if (mode == QZ_GRAM_FULL) {
+    // One launch per token segment: inside a launch every CTA sweeps the same
+    // rows at about the same time, so the column panels they share stay in L2;
+    // segments accumulate in stream order (deterministic, exactly symmetric).
+    p.tiles_n = (K + 255) / 256;
     int64_t n = 0;
-    for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / kBN;
+    for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
     p.n_tiles = n;
-    return launch_gemm<kGramFull>(map, map, map, p, st);
+    const int64_t seg = gram_segment_rows();
+    for (int64_t t0 = 0; t0 < T; t0 += seg) {
+      const int64_t rows = T - t0 < seg ? T - t0 : seg;
+      CUtensorMap map;
+      s = make_map(&map, X + t0 * K, (uint64_t)K, (uint64_t)rows, 64, 64);
+      if (s != QZ_OK) return s;
+      p.T = rows;
+      p.accumulate = (t0 > 0) || accumulate;
+      s = launch_gemm<kGramFull>(map, map, map, p, st);
+      if (s != QZ_OK) return s;
+    }
+    return QZ_OK;
   }
-  p.n_tiles = p.tiles_m;
-  return launch_gemm<kGramDiag>(map, map, map, p, st);
+  // Block-diagonal: (split, diagonal tile) units; split 0 writes H, the others
+  // write scratch partials that one more pass adds in split order.
+  CUtensorMap map;
+  s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
+  if (s != QZ_OK) return s;
+  p.T = T;
+  p.accumulate = accumulate;
+  p.tiles_n = 1;
+  int64_t splits = (8 * (int64_t)sms + p.tiles_m - 1) / p.tiles_m;
+  const int64_t max_splits = (T + 4095) / 4096;  // keep >= 4096 rows per unit
+  splits = splits < max_splits ? splits : max_splits;
+  if (splits < 1) splits = 1;
+  p.split_rows = ((T + splits - 1) / splits + kBK - 1) / kBK * kBK;
+  splits = (T + p.split_rows - 1) / p.split_rows;
+  p.splits = splits;
+  p.n_tiles = p.tiles_m * splits;
+  const size_t part_elems = (size_t)K * block_size;
+  float* parts = nullptr;
+  if (splits > 1) {
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&parts), (splits - 1) * part_elems * 4, st);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMallocAsync (gram partials)");
+  }
+  p.partials = parts;
+  s = launch_gemm<kGramDiag>(map, map, map, p, st);
+  if (s == QZ_OK && splits > 1) {
+    const int64_t n4 = (int64_t)part_elems / 4;
+    add_partials_kernel<<<(unsigned)(sms * 4), 256, 0, st>>>(reinterpret_cast<float4*>(H),
+                                                              reinterpret_cast<const float4*>(parts), n4,
+                                                              splits - 1);
+    s = cuda_status(cudaGetLastError(), "add_partials launch");
+  }
+  if (parts) cudaFreeAsync(parts, st);
+  return s;
 }
 
 extern "C" int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, const uint16_t* W,
