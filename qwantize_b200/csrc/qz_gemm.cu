@@ -64,6 +64,9 @@ struct GemmParams {
   int accumulate;       // add into H instead of storing
   int64_t tiles_m, tiles_n, n_tiles;
   int64_t splits, split_rows;  // kGramDiag: T is cut into `splits` ranges of split_rows
+  int64_t seg_rows, band;      // kGramFull: token rows per segment, tile rows per band
+  int* seq;                    // kGramFull: per-tile count of segments already added
+  int64_t tiles_per_seg;       // kGramFull: tiles in one segment (units = tiles x segments)
   float* H;
   float* partials;      // kGramDiag: splits-1 partial (K/bs, bs, bs) buffers
   double* sums;
@@ -157,30 +160,53 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64
     nj = t % p.tiles_n;
     return;
   }
-  // kGramFull: rows mi = 0.., in each row the n-tiles with nj*256 + 255 >= mi*128
-  // (the first is (mi*128)/256); rows are enumerated in order.
+  // kGramFull: tiles (mi, nj) with nj*256 + 255 >= mi*128, enumerated in bands
+  // of p.band tile rows, column by column inside a band, so the ~148 tiles in
+  // flight share few column panels of X (L2 reuse).
   int64_t r = t;
-  int64_t row = 0;
-  while (true) {
-    int64_t first = (row * kBM) / 256;
-    int64_t cnt = p.tiles_n - first;
-    if (r < cnt) { mi = row; nj = first + r; return; }
-    r -= cnt;
-    ++row;
+  for (int64_t b0 = 0; b0 < p.tiles_m; b0 += p.band) {
+    const int64_t rows_end = b0 + p.band < p.tiles_m ? b0 + p.band : p.tiles_m;
+    for (int64_t n = (b0 * kBM) / 256; n < p.tiles_n; ++n) {
+      const int64_t hi = rows_end < 2 * n + 2 ? rows_end : 2 * n + 2;  // rows with mi/2 <= n
+      const int64_t cnt = hi - b0;
+      if (r < cnt) { mi = b0 + r; nj = n; return; }
+      r -= cnt;
+    }
   }
+  mi = nj = 0;
 }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// Rows [r0, r1) of X that unit t reduces over (Gram), or K-steps (metrics).
+// A work unit: output tile (mi, nj), the rows [r0, r0 + 64*steps) of X it
+// reduces over (Gram) or its K-steps (metrics), and for the full Gram the tile
+// id and segment (units run segment-major: every segment's tiles, in order).
+struct Unit {
+  int64_t mi, nj, r0, steps, tile, seg;
+};
+
 template <int MODE>
-__device__ __forceinline__ int64_t unit_steps(const GemmParams& p, int64_t nj, int64_t& r0) {
-  if (MODE == kMetrics) { r0 = 0; return (p.K + kBK - 1) / kBK; }
-  if (MODE == kGramFull) { r0 = 0; return (p.T + kBK - 1) / kBK; }
-  r0 = nj * p.split_rows;
-  int64_t r1 = r0 + p.split_rows < p.T ? r0 + p.split_rows : p.T;
-  return (r1 - r0 + kBK - 1) / kBK;
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t t) {
+  Unit u{};
+  if (MODE == kMetrics) {
+    tile_coords(p, MODE, t, u.mi, u.nj);
+    u.steps = (p.K + kBK - 1) / kBK;
+    return u;
+  }
+  if (MODE == kGramDiag) {
+    tile_coords(p, MODE, t, u.mi, u.nj);  // nj = split index
+    u.r0 = u.nj * p.split_rows;
+  } else {
+    u.seg = t / p.tiles_per_seg;
+    u.tile = t % p.tiles_per_seg;
+    tile_coords(p, MODE, u.tile, u.mi, u.nj);
+    u.r0 = u.seg * p.seg_rows;
+  }
+  const int64_t rows = MODE == kGramDiag ? p.split_rows : p.seg_rows;
+  const int64_t r1 = u.r0 + rows < p.T ? u.r0 + rows : p.T;
+  u.steps = (r1 - u.r0 + kBK - 1) / kBK;
+  return u;
 }
 
 template <int MODE>
@@ -231,9 +257,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x) {
-        int64_t mi, nj, r0;
-        tile_coords(p, MODE, t, mi, nj);
-        const int64_t k_steps = unit_steps<MODE>(p, nj, r0);
+        const Unit u = unit_of<MODE>(p, t);
+        const int64_t mi = u.mi, nj = u.nj, r0 = u.r0, k_steps = u.steps;
         for (int64_t ks = 0; ks < k_steps; ++ks, ++it) {
           const int s = it % G::kStages;
           if (!wait(empty + s, ((it / G::kStages) & 1) ^ 1, kDevErrLoadTimeout)) goto producer_done;
@@ -267,9 +292,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t idesc = instr_desc(kBM, BN, mn, mn);
       uint32_t it = 0, lt = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
-        int64_t mi, nj, r0;
-        tile_coords(p, MODE, t, mi, nj);
-        const int64_t k_steps = unit_steps<MODE>(p, nj, r0);
+        const int64_t k_steps = unit_of<MODE>(p, t).steps;
         const uint32_t acc = lt & 1;
         if (!wait(tempty + acc, ((lt >> 1) & 1) ^ 1, kDevErrMmaTimeout)) break;
         tc_fence_after();
@@ -306,8 +329,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t lt = 0;
     double part0 = 0.0, part1 = 0.0;
     for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
-      int64_t mi, nj;
-      tile_coords(p, MODE, t, mi, nj);
+      const Unit u = unit_of<MODE>(p, t);
+      const int64_t mi = u.mi, nj = u.nj;
       const uint32_t acc = lt & 1;
       if (!wait(tfull + acc, (lt >> 1) & 1, kDevErrEpilogueTimeout)) break;
       tc_fence_after();
@@ -354,6 +377,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
+        // segments of one tile are added in order: wait until the previous
+        // segment of this tile has been written (bounded), add, then publish
+        bool go = true;
+        if (lane == 0) {
+          const volatile int* sq = p.seq + u.tile;
+          if (*sq < u.seg) {
+            const uint64_t t0 = globaltimer_ns();
+            while (*sq < u.seg) {
+              if (*abort_s) { go = false; break; }
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&qz_device_error, kDevErrEpilogueTimeout);
+                *abort_s = 1;
+                go = false;
+                break;
+              }
+              __nanosleep(256);
+            }
+          }
+        }
+        go = __shfl_sync(0xffffffffu, go, 0);
+        if (!go) break;
+        __threadfence();
+        const bool add = u.seg > 0 || p.accumulate;
         const int64_t i = mi * kBM + row;
         const int64_t j0 = nj * BN;
 #pragma unroll 1
@@ -368,7 +414,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-              if (p.accumulate) {
+              if (add) {
                 float4 o = up[q];
                 w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
               }
@@ -383,12 +429,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const int64_t j = jc + q;
               if (j >= p.K || j < i) continue;
               float* up = p.H + i * p.K + j;
-              const float val = p.accumulate ? v[q] + *up : v[q];
+              const float val = add ? v[q] + *up : v[q];
               *up = val;
               if (j > i) p.H[j * p.K + i] = val;
             }
           }
         }
+      }
+      if (MODE == kGramFull) {
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+        if (warp == 2 && lane == 0) atomicExch(p.seq + u.tile, (int)(u.seg + 1));
       }
       tc_fence_before();
       mbar_arrive(tempty + acc);
@@ -480,7 +531,7 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
 
 // Token rows per full-Gram launch (QZ_GRAM_SEGMENT overrides; a multiple of 64).
 static int64_t gram_segment_rows() {
-  int64_t seg = 65536;
+  int64_t seg = 262144;
   if (const char* v = getenv("QZ_GRAM_SEGMENT")) seg = atoll(v);
   if (seg < 64) seg = 64;
   return seg / 64 * 64;
@@ -530,25 +581,32 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   int s = current_sms(&sms);
   if (s != QZ_OK) return s;
   if (mode == QZ_GRAM_FULL) {
-    // One launch per token segment: inside a launch every CTA sweeps the same
-    // rows at about the same time, so the column panels they share stay in L2;
-    // segments accumulate in stream order (deterministic, exactly symmetric).
+    // One persistent launch over (segment, tile) units, segment-major: all CTAs
+    // sweep the same token rows at about the same time, so the column panels
+    // they share stay in L2.  A tile's segments are added in segment order
+    // (per-tile counters in scratch), so H is deterministic and exactly symmetric.
     p.tiles_n = (K + 255) / 256;
     int64_t n = 0;
     for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
-    p.n_tiles = n;
-    const int64_t seg = gram_segment_rows();
-    for (int64_t t0 = 0; t0 < T; t0 += seg) {
-      const int64_t rows = T - t0 < seg ? T - t0 : seg;
-      CUtensorMap map;
-      s = make_map(&map, X + t0 * K, (uint64_t)K, (uint64_t)rows, 64, 64);
-      if (s != QZ_OK) return s;
-      p.T = rows;
-      p.accumulate = (t0 > 0) || accumulate;
-      s = launch_gemm<kGramFull>(map, map, map, p, st);
-      if (s != QZ_OK) return s;
-    }
-    return QZ_OK;
+    p.tiles_per_seg = n;
+    p.seg_rows = gram_segment_rows();
+    const int64_t n_segs = (T + p.seg_rows - 1) / p.seg_rows;
+    p.n_tiles = n * n_segs;
+    p.band = 4;
+    if (const char* v = getenv("QZ_GRAM_BAND")) p.band = atoll(v) > 0 ? atoll(v) : 4;
+    p.T = T;
+    p.accumulate = accumulate;
+    CUtensorMap map;
+    s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
+    if (s != QZ_OK) return s;
+    int* seq = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&seq), (size_t)n * sizeof(int), st);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMallocAsync (gram tile counters)");
+    e = cudaMemsetAsync(seq, 0, (size_t)n * sizeof(int), st);
+    p.seq = seq;
+    s = e == cudaSuccess ? launch_gemm<kGramFull>(map, map, map, p, st) : cuda_status(e, "cudaMemsetAsync");
+    cudaFreeAsync(seq, st);
+    return s;
   }
   // Block-diagonal: (split, diagonal tile) units; split 0 writes H, the others
   // write scratch partials that one more pass adds in split order.
