@@ -121,6 +121,25 @@ QZ_API int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int block_
             float* H, void* stream);
 
 /*
+ * qz_gram_full_noalloc -- the full Gram H = X^T X of qz_gram (QZ_GRAM_FULL),
+ * for callers that must not allocate device memory during the call, e.g. code
+ * running inside a framework's own memory pool or allocator hook, or a host
+ * program that has handed all device memory to another component.  qz_gram
+ * allocates a small per-call counter buffer (cudaMallocAsync); this entry point
+ * keeps those counters in a fixed 256 KB device array inside the library
+ * instead, so it calls no allocator at all.  No counterpart in the reference.
+ *   - Limit: at most 65,536 output tiles of 128 x 256, i.e. K <= 65280; larger
+ *     K is rejected with QZ_ERR_INVALID before any device work.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the one array (zeroed at the start of each call): calls
+ *     that can overlap on the GPU, on any stream, race and must be serialised.
+ *   - Every GPU that loads the library keeps the array until the process exits.
+ */
+QZ_API int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int accumulate, float* H,
+                                void* stream);
+
+/*
  * qz_weight_error_sums -- sums[0] += sum (W_dq - W)^2, sums[1] += sum W^2 in
  * double (metrics.py:23-27).  W and W_dq are n elements of w_dtype / dq_dtype.
  */

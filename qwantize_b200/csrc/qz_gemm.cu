@@ -27,6 +27,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/qwantize_b200.h"
 #include "qz_kernels.h"
@@ -545,6 +546,35 @@ static void mn_offsets(uint32_t* lbo, uint32_t* sbo) {
   if (const char* v = getenv("QZ_MN_SBO")) *sbo = (uint32_t)atoi(v);
 }
 
+// ---------------------------------------------------------------------------
+// Fixed scratch for qz_gram_full_noalloc: the full Gram's per-tile segment
+// counters live in this file-scope device array instead of memory the call
+// allocates.  Every device that loads the library holds it (256 KB) until exit.
+// ---------------------------------------------------------------------------
+constexpr int64_t kNoAllocMaxTiles = 65536;
+static __device__ __align__(256) int g_noalloc_tile_counters[kNoAllocMaxTiles];
+
+// Device address of the array for the current device.  In host code the
+// array's name is only a stand-in, so the address is looked up once per device
+// (with that device current) and cached.
+static int noalloc_counters(int** out) {
+  static std::mutex mu;
+  static int* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(QZ_ERR_INVALID, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_tile_counters);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress (no-alloc scratch)");
+    addr[dev] = static_cast<int*>(p);
+  }
+  *out = addr[dev];
+  return QZ_OK;
+}
+
 cudaError_t read_device_error_gemm(unsigned* out, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(out, qz_device_error, sizeof(unsigned));
   if (e != cudaSuccess || !clear) return e;
@@ -664,4 +694,47 @@ extern "C" int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, con
   p.tiles_n = (M + 127) / 128;
   p.n_tiles = p.tiles_m * p.tiles_n;
   return launch_gemm<kMetrics>(mx, mw, mq, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int accumulate, float* H,
+                                    void* stream) {
+  if (T < 0 || K <= 0) return fail(QZ_ERR_INVALID, "need T >= 0 and K > 0");
+  if (K % 8 != 0) return fail(QZ_ERR_INVALID, "K must be a multiple of 8 (16-byte rows for TMA)");
+  if (K > 2147483647LL || T > 2147483647LL) return fail(QZ_ERR_INVALID, "T and K must fit in int32");
+  if (!H) return fail(QZ_ERR_INVALID, "H is NULL");
+  GemmParams p{};
+  p.tiles_m = (K + kBM - 1) / kBM;
+  p.tiles_n = (K + 255) / 256;
+  int64_t n = 0;
+  for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
+  if (n > kNoAllocMaxTiles)
+    return fail(QZ_ERR_INVALID,
+                "qz_gram_full_noalloc: K = %lld needs %lld output tiles; the fixed scratch holds %lld "
+                "(K <= 65280); use qz_gram",
+                (long long)K, (long long)n, (long long)kNoAllocMaxTiles);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    if (accumulate) return QZ_OK;
+    return cuda_status(cudaMemsetAsync(H, 0, (size_t)K * K * 4, st), "cudaMemsetAsync");
+  }
+  if (!X) return fail(QZ_ERR_INVALID, "X is NULL");
+  if (reinterpret_cast<uintptr_t>(X) % 16) return fail(QZ_ERR_INVALID, "X must be 16-byte aligned");
+  int* counters = nullptr;
+  int s = noalloc_counters(&counters);
+  if (s != QZ_OK) return s;
+  // the counters must start at zero; the previous call left them non-zero
+  s = cuda_status(cudaMemsetAsync(counters, 0, (size_t)n * sizeof(int), st), "cudaMemsetAsync (counters)");
+  if (s != QZ_OK) return s;
+  p.K = K; p.M = 0; p.bs = 16; p.H = H; p.T = T; p.accumulate = accumulate;
+  mn_offsets(&p.lbo, &p.sbo);
+  p.tiles_per_seg = n;
+  p.seg_rows = gram_segment_rows();
+  p.n_tiles = n * ((T + p.seg_rows - 1) / p.seg_rows);
+  p.band = 4;
+  if (const char* v = getenv("QZ_GRAM_BAND")) p.band = atoll(v) > 0 ? atoll(v) : 4;
+  p.seq = counters;
+  CUtensorMap map;
+  s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
+  if (s != QZ_OK) return s;
+  return launch_gemm<kGramFull>(map, map, map, p, st);
 }
