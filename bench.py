@@ -101,8 +101,8 @@ def measured_peaks():
 
 
 def make_pool(rank, device):
-    from qwantize_b200.synthetic import make_weight
-    return [make_weight(M, K, seed=1000 * rank + i).to(device) for i in range(POOL)]
+    from qwantize_b200.synthetic import make_weight_device
+    return [make_weight_device(M, K, 1000 * rank + i, device) for i in range(POOL)]
 
 
 def alloc_outputs(device):
@@ -272,6 +272,18 @@ def bench_ours(args):
     else:
         nc = None
 
+    extra = None
+    if not args.no_extras:
+        peak_tf = 1657.2
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peak_tf = json.load(f).get("bf16_tflops", peak_tf)
+        except OSError:
+            pass
+        del pool
+        torch.cuda.empty_cache()
+        extra = extras(ws, rank, device, peak_tf)
+
     if rank == 0:
         issue = None
         if meth == 1 and nc is not None:
@@ -306,10 +318,110 @@ def bench_ours(args):
             "e2e": {"value": e2e_value, "unit": "G weights/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "clocks": clk,
+            "extras": extra,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()
+
+
+def _ev_time(fn, stream, reps=1):
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _max_over_ranks(v, ws, device):
+    if ws == 1:
+        return v
+    t = torch.tensor([v], device=device, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def extras(ws, rank, device, peak_tf):
+    """Configs 2 and 3 on the same GPUs (device-timed, max over ranks):
+    config 2: Gram of 1,048,576 x 9728 synthetic activations (tokens sharded
+    over ranks in whole 65,536-token chunks, then one NCCL all-reduce of H),
+    H-optimal search (NVFP4 and MXFP4, bs 16) of the 2560x9728 weight, and
+    compute_metrics' output-error GEMM; config 3: NVFP4 bs16 SSE-optimal over
+    the Qwen3-4B-shaped stack (3.63B weights, rows sharded over ranks)."""
+    import qwantize_b200 as q
+    from qwantize_b200 import _lib
+    from qwantize_b200.distributed import shard_range, token_chunks
+    from qwantize_b200.hessian import gram
+    from qwantize_b200.metrics import output_error_sums
+    from qwantize_b200.synthetic import (QWEN3_4B_LAYER, QWEN3_4B_LAYERS, layer_seed, make_activations,
+                                         make_weight_device)
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    T, Kx = 1048576, 9728
+    t0, t1 = token_chunks(T, ws, rank)
+    X = make_activations(t1 - t0, Kx, seed=1, device=device, t0=t0)
+    H = torch.empty(Kx, Kx, device=device)
+    Hb = torch.empty(Kx // 16, 16, 16, device=device)
+    ms_full = _max_over_ranks(_ev_time(lambda: gram(X, "full", out=H), stream), ws, device)
+    ms_diag = _max_over_ranks(_ev_time(lambda: gram(X, "blockdiag", 16, out=Hb), stream, 3), ws, device)
+    ar_ms = None
+    if ws > 1:
+        torch.distributed.barrier()
+        ar_ms = _max_over_ranks(_ev_time(lambda: torch.distributed.all_reduce(H), stream, 3), ws, device)
+    flop = T * Kx * (Kx + 1)
+    out["config2_gram"] = {
+        "tokens": T, "K": Kx, "ms_full": ms_full, "tflops_full": flop / ms_full / 1e9,
+        "frac_of_measured_bf16_peak": flop / ms_full / 1e9 / peak_tf,
+        "ms_blockdiag": ms_diag, "blockdiag_GBps": 2 * (t1 - t0) * Kx / ms_diag / 1e6,
+        "allreduce_full_H_ms": ar_ms, "sharding": f"tokens over {ws} rank(s), whole 65536-token chunks"}
+    W = make_weight_device(2560, Kx, 0, device)
+    Wb = W.reshape(2560, Kx // 16, 16)
+    Hbd = Hb  # the search uses the block diagonal, all-reduced over ranks when N > 1
+    if ws > 1:
+        torch.distributed.all_reduce(Hbd)
+    ms_nv = _ev_time(lambda: q.nvfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    ms_mx = _ev_time(lambda: q.mxfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    _, _, dq = q.nvfp4_optimal(Wb, return_dequant=True)
+    dqb = dq.reshape(2560, Kx).to(torch.bfloat16)
+    ms_m = _max_over_ranks(_ev_time(lambda: output_error_sums(W, dqb, X), stream), ws, device)
+    mflop = 4 * (t1 - t0) * Kx * 2560
+    out["config2_hopt"] = {
+        "weights": 2560 * Kx, "nvfp4_bs16_search_ms": ms_nv, "mxfp4_bs16_search_ms": ms_mx,
+        "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
+        "metrics_output_error_ms": ms_m, "metrics_tflops": mflop / ms_m / 1e9}
+    del X, H
+    torch.cuda.empty_cache()
+    # config 3: the Qwen3-4B stack, rows sharded
+    mats = []
+    n_local = 0
+    for layer in range(QWEN3_4B_LAYERS):
+        for name, Mo, Ki in QWEN3_4B_LAYER:
+            r0, r1 = shard_range(Mo, ws, rank)
+            mats.append(make_weight_device(r1 - r0, Ki, layer_seed(layer, name), device))
+            n_local += (r1 - r0) * Ki
+    codes = torch.empty(max(m.numel() for m in mats) // 16, dtype=torch.uint8, device=device)
+    packed = torch.empty(max(m.numel() for m in mats) // 2, dtype=torch.uint8, device=device)
+    L = _lib.load()
+    sp = stream.cuda_stream
+
+    def stack():
+        for m in mats:
+            L.qz_quantize(m.data_ptr(), 1, m.numel() // 16, 16, 0, 1, None, 0, None, None, None,
+                          codes.data_ptr(), packed.data_ptr(), None, sp)
+    ms_s = _max_over_ranks(_ev_time(stack, stream, 2), ws, device)
+    n_total = n_local
+    if ws > 1:
+        t = torch.tensor([n_local], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t)
+        n_total = int(t.item())
+    out["config3_qwen3_4b_stack"] = {
+        "weights": n_total, "ms": ms_s, "gweights_per_s": n_total / (ms_s / 1e3) / 1e9,
+        "method": "nvfp4 bs16 SSE-optimal, scale bytes + packed codes", "sharding": f"rows over {ws} rank(s)"}
+    return out
 
 
 def main():
@@ -319,6 +431,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip configs 2 and 3")
     args = ap.parse_args()
     if args.impl == "reference":
         bench_reference(args)
