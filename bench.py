@@ -46,29 +46,59 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """SM clock and throttle reasons sampled every 20 ms while the timed region
+    runs (NVML, read-only; nvidia-smi every 200 ms if NVML is unavailable)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event-reason bits
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4}
 
-    def __init__(self, index):
-        self.index = index
-        self.samples = []
+    def __init__(self, cuda_index):
+        self.index = cuda_index
+        self.samples = []  # (sm_mhz, max_mhz, reason_bits)
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            ids = [v for v in vis.split(",") if v.strip()]
+            phys = int(ids[cuda_index]) if ids and ids[cuda_index].strip().isdigit() else cuda_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self._nvml = pynvml
+        except Exception:
+            self._nvml = None
+
+    def _sample(self):
+        n = self._nvml
+        if n is not None:
+            sm = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+            mx = n.nvmlDeviceGetMaxClockInfo(self._h, n.NVML_CLOCK_SM)
+            try:
+                rs = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                rs = n.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+            return sm, mx, rs
+        out = subprocess.run(["nvidia-smi", f"--id={self.index}", "--query-gpu=clocks.sm,clocks.max.sm,"
+                              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                             timeout=5).stdout.strip().split(",")
+        bits = 0
+        for name, v in zip(("hw_slowdown", "sw_thermal_slowdown", "hw_thermal_slowdown", "sw_power_cap"), out[2:]):
+            if "Active" in v and "Not" not in v:
+                bits |= self.REASONS[name]
+        return float(out[0]), float(out[1]), bits
 
     def _run(self):
+        period = 0.02 if self._nvml is not None else 0.2
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True,
-                                     text=True, timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([c.strip() for c in out.split(",")])
+                self.samples.append(self._sample())
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(period)
 
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
@@ -81,14 +111,11 @@ class ClockSampler:
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for s in self.samples for n, v in zip(names, s[5:9]) if "Active" in v and "Not" not in v})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"], "samples": 0}
+        reasons = sorted({k for _, _, b in self.samples for k, bit in self.REASONS.items() if b & bit})
+        return {"sm_mhz": float(np.median([s[0] for s in self.samples])),
+                "sm_max_mhz": float(max(s[1] for s in self.samples)), "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 def measured_peaks():
@@ -231,35 +258,33 @@ def bench_ours(args):
     achieved = WEIGHTS * bytes_per_w / (per[dom] / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
 
-    # ---- end to end through the public API, host (pinned) buffers ----
-    import qwantize_b200 as q
-    host_pool = [p.cpu().pin_memory() for p in pool[:2]]
-    h2d = d2h = 0
+    # ---- end to end through the public API from host (pinned) buffers ----
+    # qwantize_b200.pipeline.HostBatchQuantizer: H2D copy, kernel and D2H copy
+    # of consecutive calls overlap on three streams; every step copies each of
+    # its 8 inputs in and its native outputs (scale bytes, nibbles, bf16
+    # dequant) out.
+    from qwantize_b200.pipeline import HostBatchQuantizer
+    host_pool = [p.cpu().pin_memory() for p in pool]
+    hq = HostBatchQuantizer(WEIGHTS, device=device, slots=3)
+    items = [(host_pool[k].reshape(M, K // b, b), FMT_NAME[f], METH_NAME[m], b)
+             for k, (f, b, m) in enumerate(CALLS)]
+    outs_h = [(torch.empty(WEIGHTS // b, dtype=torch.uint8, pin_memory=True),
+               torch.empty(WEIGHTS // 2, dtype=torch.uint8, pin_memory=True),
+               torch.empty(WEIGHTS, dtype=torch.bfloat16, pin_memory=True)) for (_, _, _, b) in items]
+    h2d = sum(w.numel() * 2 for (w, _, _, _) in items)
+    d2h = sum(sum(t.numel() * t.element_size() for t in o) for o in outs_h)
+    hq.run_items(items, outs_h)  # warm-up
     torch.cuda.synchronize(device)
     barrier()
+    e2e_steps = max(3, min(args.steps, 10))
     t0 = time.perf_counter()
-    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ee0.record(stream)
-    e2e_steps = max(1, min(args.steps, 3))
-    for s in range(e2e_steps):
-        for k, (f, b, m) in enumerate(CALLS):
-            Wh = host_pool[k % 2]
-            Wd = Wh.to(device, non_blocking=True).reshape(M, K // b, b)
-            fn = q.nvfp4_quantize_packed if f == 0 else q.mxfp4_quantize_packed
-            codes, packed, dqb = fn(Wd, method=METH_NAME[m], return_dequant=True)
-            res = [t.to("cpu", non_blocking=True) for t in (codes, packed, dqb)]
-            if s == 0:
-                h2d += Wh.numel() * 2
-                d2h += sum(t.numel() * t.element_size() for t in (codes, packed, dqb))
-    ee1.record(stream)
+    for _ in range(e2e_steps):
+        hq.run_items(items, outs_h)
     torch.cuda.synchronize(device)
-    del res
-    e2e_ms = ee0.elapsed_time(ee1)
-    if ws > 1:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    e2e_ms = _max_over_ranks(e2e_ms, ws, device)
     e2e_value = WEIGHTS * len(CALLS) * e2e_steps * ws / (e2e_ms / 1e3) / 1e9
+    del host_pool, hq
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -282,7 +307,7 @@ def bench_ours(args):
             pass
         del pool
         torch.cuda.empty_cache()
-        extra = extras(ws, rank, device, peak_tf)
+        extra = extras(ws, rank, device, peak_tf, args.gram_tokens, args.stack_layers)
 
     if rank == 0:
         issue = None
@@ -316,7 +341,8 @@ def bench_ours(args):
                          "bytes_per_weight": bytes_per_w, "issue": issue},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "G weights/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": "qwantize_b200.pipeline.HostBatchQuantizer (pinned host in/out, 3 overlapping streams), host wall clock"},
             "clocks": clk,
             "extras": extra,
         }
@@ -345,7 +371,7 @@ def _max_over_ranks(v, ws, device):
     return float(t.item())
 
 
-def extras(ws, rank, device, peak_tf):
+def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
     """Configs 2 and 3 on the same GPUs (device-timed, max over ranks):
     config 2: Gram of 1,048,576 x 9728 synthetic activations (tokens sharded
     over ranks in whole 65,536-token chunks, then one NCCL all-reduce of H),
@@ -361,7 +387,7 @@ def extras(ws, rank, device, peak_tf):
                                          make_weight_device)
     stream = torch.cuda.current_stream(device)
     out = {}
-    T, Kx = 1048576, 9728
+    Kx = 9728
     t0, t1 = token_chunks(T, ws, rank)
     X = make_activations(t1 - t0, Kx, seed=1, device=device, t0=t0)
     H = torch.empty(Kx, Kx, device=device)
@@ -398,7 +424,7 @@ def extras(ws, rank, device, peak_tf):
     # config 3: the Qwen3-4B stack, rows sharded
     mats = []
     n_local = 0
-    for layer in range(QWEN3_4B_LAYERS):
+    for layer in range(min(n_layers, QWEN3_4B_LAYERS)):
         for name, Mo, Ki in QWEN3_4B_LAYER:
             r0, r1 = shard_range(Mo, ws, rank)
             mats.append(make_weight_device(r1 - r0, Ki, layer_seed(layer, name), device))
@@ -427,11 +453,15 @@ def extras(ws, rank, device, peak_tf):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip configs 2 and 3")
+    ap.add_argument("--gram-tokens", type=int, default=1048576,
+                    help="tokens for the config-2 extras (smaller for profiling runs)")
+    ap.add_argument("--stack-layers", type=int, default=36,
+                    help="layers of the config-3 stack (smaller for profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         bench_reference(args)

@@ -197,3 +197,22 @@ def test_weight_metrics():
     ref = g["without_x"]
     assert abs(r["weight_error"] - ref[0]) <= 1e-5 * ref[0]
     assert abs(r["weight_error_pct"] - ref[1]) <= 1e-5 * ref[1]
+
+
+def test_host_pipeline_matches_device_path():
+    """HostBatchQuantizer (host in/out, overlapping streams) returns exactly the
+    native outputs of the device-resident call."""
+    from qwantize_b200.pipeline import HostBatchQuantizer
+    from qwantize_b200.synthetic import make_weight
+    m = q()
+    ws = [make_weight(256, 1024, seed=40 + i).pin_memory() for i in range(5)]
+    specs = [("nvfp4", "optimal", 16), ("mxfp4", "naive", 32), ("nvfp4", "naive", 32),
+             ("mxfp4", "optimal", 16), ("nvfp4", "optimal", 32)]
+    hq = HostBatchQuantizer(256 * 1024, slots=2)
+    res = hq.run_items([(w, f, me, b) for w, (f, me, b) in zip(ws, specs)])
+    for w, (f, me, b), (codes, packed, dq) in zip(ws, specs, res):
+        fn = m.nvfp4_quantize_packed if f == "nvfp4" else m.mxfp4_quantize_packed
+        c2, p2, d2 = fn(w.to(DEV).reshape(-1, b), method=me, return_dequant=True)
+        assert torch.equal(codes, c2.cpu().reshape(-1))
+        assert torch.equal(packed, p2.cpu().reshape(-1))
+        assert torch.equal(dq.view(torch.int16), d2.cpu().reshape(-1).view(torch.int16))
