@@ -257,6 +257,11 @@ def bench_ours(args):
     bytes_per_w = 2 + 0.5 + 1.0 / bs + 2  # bf16 in; nibbles + scale byte + bf16 dequant out
     achieved = WEIGHTS * bytes_per_w / (per[dom] / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
+    # DRAM read + write bytes of one launch of the dominant kernel (NVFP4 bs16
+    # SSE, native outputs) from one ncu capture (profiles/
+    # quantize_nvfp4_sse_bs16_config1.md): 49.85 MB read + 9.56 MB written
+    # (most of the 63.8 MB of outputs is still in L2 when the kernel ends).
+    traffic = 59.41e6 if dom == (0, 16, 1) else None
 
     # ---- end to end through the public API from host (pinned) buffers ----
     # qwantize_b200.pipeline.HostBatchQuantizer: H2D copy, kernel and D2H copy
@@ -337,7 +342,7 @@ def bench_ours(args):
             "per_kernel_ms": {f"{FMT_NAME[f]}_{METH_NAME[m]}_bs{b}": v for (f, b, m), v in per.items()},
             "roofline": {"kernel": f"quantize {FMT_NAME[fmt]} {METH_NAME[meth]} bs{bs}", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind, "traffic": traffic, "traffic_unit": "bytes per launch (ncu)",
                          "bytes_per_weight": bytes_per_w, "issue": issue},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "G weights/s", "h2d_bytes_per_step": h2d,
@@ -400,8 +405,9 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         ar_ms = _max_over_ranks(_ev_time(lambda: torch.distributed.all_reduce(H), stream, 3), ws, device)
     flop = T * Kx * (Kx + 1)
     out["config2_gram"] = {
-        "tokens": T, "K": Kx, "ms_full": ms_full, "tflops_full": flop / ms_full / 1e9,
-        "frac_of_measured_bf16_peak": flop / ms_full / 1e9 / peak_tf,
+        "tokens": T, "K": Kx, "ms_full": ms_full, "tflops_full_whole_job": flop / ms_full / 1e9,
+        "tflops_full_per_gpu": flop / ms_full / 1e9 / ws,
+        "frac_of_measured_bf16_peak": flop / ms_full / 1e9 / ws / peak_tf,
         "ms_blockdiag": ms_diag, "blockdiag_GBps": 2 * (t1 - t0) * Kx / ms_diag / 1e6,
         "allreduce_full_H_ms": ar_ms, "sharding": f"tokens over {ws} rank(s), whole 65536-token chunks"}
     W = make_weight_device(2560, Kx, 0, device)
@@ -418,7 +424,7 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
     out["config2_hopt"] = {
         "weights": 2560 * Kx, "nvfp4_bs16_search_ms": ms_nv, "mxfp4_bs16_search_ms": ms_mx,
         "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
-        "metrics_output_error_ms": ms_m, "metrics_tflops": mflop / ms_m / 1e9}
+        "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9}
     del X, H
     torch.cuda.empty_cache()
     # config 3: the Qwen3-4B stack, rows sharded
