@@ -96,27 +96,81 @@ __device__ __forceinline__ float block_sse(const float (&a)[BS], float s) {
   return sum8<BS>(d2);
 }
 
-// Block SSE with hardware rounding: bf16/fp16 inputs, finite s > 0.
+// Block SSE with hardware rounding: bf16/fp16 inputs, finite s > 0, with
+// c = RN(RN(1/s) * (1 - 2^-13)) precomputed.  d = a - q*s is one FMA: q*s is
+// exact in fp32 (q has <= 2 significant bits, s <= 4, and a UE8M0 product that
+// overflows is infinite in both forms), so the single rounding of the FMA equals
+// the reference's rounding of a - dq.
 template <int BS>
-__device__ __forceinline__ float block_sse_hw(const float (&a)[BS], float s) {
-  const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
+__device__ __forceinline__ float block_sse_hw(const float (&a)[BS], float s, float c) {
   float d2[BS];
 #pragma unroll
   for (int i = 0; i < BS; i += 2) {
     const float2 q = e2m1x2_to_float2(e2m1x2_rn(__fmul_rn(a[i], c), __fmul_rn(a[i + 1], c)));
-    const float d0 = __fsub_rn(a[i], __fmul_rn(q.x, s));
-    const float d1 = __fsub_rn(a[i + 1], __fmul_rn(q.y, s));
+    const float d0 = __fmaf_rn(-q.x, s, a[i]);
+    const float d1 = __fmaf_rn(-q.y, s, a[i + 1]);
     d2[i] = __fmul_rn(d0, d0);
     d2[i + 1] = __fmul_rn(d1, d1);
   }
   return sum8<BS>(d2);
 }
 
+// NVFP4 variant: the decoded codes stay in f16 and feed a mixed-precision FMA
+// (f16 x f16 + f32 -> f32): d = RN(a - q*s) with -s held exactly in f16 (every
+// E4M3 value is a normal f16), saving the f16 -> f32 conversions.
+__device__ __forceinline__ float2 fma2_f16(uint32_t q_h2, uint32_t neg_s_h, float a0, float a1) {
+  float d0, d1;
+  asm("{\n .reg .b16 lo, hi, s;\n mov.b32 {lo, hi}, %2;\n cvt.u16.u32 s, %3;\n"
+      " fma.rn.f32.f16 %0, lo, s, %4;\n fma.rn.f32.f16 %1, hi, s, %5;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "r"(q_h2), "r"(neg_s_h), "f"(a0), "f"(a1));
+  return make_float2(d0, d1);
+}
+
+__device__ __forceinline__ uint32_t e2m1x2_to_half2_bits(uint32_t byte) {
+  uint32_t h2;
+  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}\n" : "=r"(h2) : "r"(byte));
+  return h2;
+}
+
+template <int BS>
+__device__ __forceinline__ float block_sse_hw_nv(const float (&a)[BS], uint32_t neg_s_h, float c) {
+  float d2[BS];
+#pragma unroll
+  for (int i = 0; i < BS; i += 2) {
+    const uint32_t q = e2m1x2_to_half2_bits(e2m1x2_rn(__fmul_rn(a[i], c), __fmul_rn(a[i + 1], c)));
+    const float2 d = fma2_f16(q, neg_s_h, a[i], a[i + 1]);
+    d2[i] = __fmul_rn(d.x, d.x);
+    d2[i + 1] = __fmul_rn(d.y, d.y);
+  }
+  return sum8<BS>(d2);
+}
+
+// Per-CTA table of candidate scales and their biased reciprocals, indexed by
+// E4M3 code (1..126) or UE8M0 biased exponent (1..254).
+struct CandTable {
+  float val[256];
+  float c[256];
+  uint32_t neg_h[256];  // f16 bits of -val (NVFP4)
+};
+
+template <int FMT>
+__device__ __forceinline__ void fill_cand_table(CandTable& t) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    const bool ok = FMT == kNVFP4 ? (i >= 1 && i <= 126) : (i >= 1 && i <= 254);
+    const float v = ok ? (FMT == kNVFP4 ? e4m3_value(i) : pow2f(i - 127)) : 1.0f;
+    t.val[i] = v;
+    t.c[i] = __fmul_rn(__frcp_rn(v), kBiasDown);
+    t.neg_h[i] = FMT == kNVFP4 ? (uint32_t)__half_as_ushort(__float2half_rn(-v)) : 0u;
+  }
+}
+
 // Candidate SSE: the hardware path for 16-bit inputs, IEEE division for fp32.
-template <int BS, int MODE, int DT>
-__device__ __forceinline__ float cand_sse(const float (&a)[BS], float s) {
-  if constexpr (DT != kDtF32) return block_sse_hw<BS>(a, s);
-  else return block_sse<BS, MODE>(a, s);
+template <int BS, int MODE, int DT, int FMT>
+__device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
+  if constexpr (DT != kDtF32 && FMT == kNVFP4) return block_sse_hw_nv<BS>(a, t.neg_h[code], t.c[code]);
+  else if constexpr (DT != kDtF32) return block_sse_hw<BS>(a, t.val[code], t.c[code]);
+  else return block_sse<BS, MODE>(a, t.val[code]);
 }
 
 // Clipping error sum(clamp(|x| - 6 s, 0)^2) (nvfp4/reference.py:209).
@@ -424,7 +478,12 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
   constexpr int MODE = Mode<FMT, DT>::v;
   constexpr int S = G::kStages;
   extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ CandTable ctab;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (METHOD == kSSE) {
+    fill_cand_table<FMT>(ctab);
+    __syncthreads();
+  }
   unsigned char* wbase = smem_raw + warp * G::kBytesAligned;
   unsigned char* stage = wbase;                                  // S x chunk
   float* rows = reinterpret_cast<float*>(wbase + S * G::kChunkBytes);  // 32 x BS |x|
@@ -491,9 +550,8 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
         float best_E = E0;
 #pragma unroll 1
         for (int c = lo; c <= hi; ++c) {
-          const float sc = cand_value<FMT>(c);
-          const float E = cand_sse<BS, MODE, DT>(a, sc);
-          if (E < best_E) { best_E = E; s = sc; }
+          const float E = cand_sse<BS, MODE, DT, FMT>(a, ctab, c);
+          if (E < best_E) { best_E = E; s = ctab.val[c]; }
         }
       }
     } else if constexpr (METHOD == kSSE) {
@@ -532,12 +590,12 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
           float4 t = r4[v];
           ar[4 * v] = t.x; ar[4 * v + 1] = t.y; ar[4 * v + 2] = t.z; ar[4 * v + 3] = t.w;
         }
-        const float E = cand_sse<BS, MODE, DT>(ar, cand_value<FMT>(c));
+        const float E = cand_sse<BS, MODE, DT, FMT>(ar, ctab, c);
         atomicMin(best + bb, ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)c);
       }
       __syncwarp();
       const unsigned win = (unsigned)(best[lane] & 0xffffffffu);
-      if (win != 0) s = cand_value<FMT>((int)win);
+      if (win != 0) s = ctab.val[win];
       __syncwarp();  // rows/best are rewritten by the next chunk
     } else if constexpr (METHOD == kTwoArgmin) {
       if (valid && !s_nan) {
