@@ -145,27 +145,65 @@ __device__ __forceinline__ float sum8(const float (&v)[BS]) {
   return r;
 }
 
-// In-register ascending bitonic sort of non-negative float bit patterns
-// (NaN patterns sort last, like torch.sort).
+// In-register ascending sort of non-negative float bit patterns (NaN patterns
+// compare above inf, so they sort last, like torch.sort): Batcher odd-even
+// merge networks, 63 compare-exchanges for 16 inputs and 191 for 32.
+#define QZ_CE(i, j)                   \
+  {                                   \
+    const uint32_t a_ = v[i], b_ = v[j]; \
+    v[i] = min(a_, b_);               \
+    v[j] = max(a_, b_);               \
+  }
 template <int N>
-__device__ __forceinline__ void bitonic_sort_u32(uint32_t (&v)[N]) {
-#pragma unroll
-  for (int k = 2; k <= N; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        int l = i ^ j;
-        if (l > i) {
-          uint32_t a = v[i], b = v[l];
-          uint32_t lo = min(a, b), hi = max(a, b);
-          if ((i & k) == 0) { v[i] = lo; v[l] = hi; }
-          else { v[i] = hi; v[l] = lo; }
-        }
-      }
-    }
+__device__ __forceinline__ void sort_u32(uint32_t (&v)[N]) {
+  if constexpr (N == 16) {
+    QZ_CE(0, 1); QZ_CE(2, 3); QZ_CE(0, 2); QZ_CE(1, 3); QZ_CE(1, 2); QZ_CE(4, 5);
+    QZ_CE(6, 7); QZ_CE(4, 6); QZ_CE(5, 7); QZ_CE(5, 6); QZ_CE(0, 4); QZ_CE(2, 6);
+    QZ_CE(2, 4); QZ_CE(1, 5); QZ_CE(3, 7); QZ_CE(3, 5); QZ_CE(1, 2); QZ_CE(3, 4);
+    QZ_CE(5, 6); QZ_CE(8, 9); QZ_CE(10, 11); QZ_CE(8, 10); QZ_CE(9, 11); QZ_CE(9, 10);
+    QZ_CE(12, 13); QZ_CE(14, 15); QZ_CE(12, 14); QZ_CE(13, 15); QZ_CE(13, 14); QZ_CE(8, 12);
+    QZ_CE(10, 14); QZ_CE(10, 12); QZ_CE(9, 13); QZ_CE(11, 15); QZ_CE(11, 13); QZ_CE(9, 10);
+    QZ_CE(11, 12); QZ_CE(13, 14); QZ_CE(0, 8); QZ_CE(4, 12); QZ_CE(4, 8); QZ_CE(2, 10);
+    QZ_CE(6, 14); QZ_CE(6, 10); QZ_CE(2, 4); QZ_CE(6, 8); QZ_CE(10, 12); QZ_CE(1, 9);
+    QZ_CE(5, 13); QZ_CE(5, 9); QZ_CE(3, 11); QZ_CE(7, 15); QZ_CE(7, 11); QZ_CE(3, 5);
+    QZ_CE(7, 9); QZ_CE(11, 13); QZ_CE(1, 2); QZ_CE(3, 4); QZ_CE(5, 6); QZ_CE(7, 8);
+    QZ_CE(9, 10); QZ_CE(11, 12); QZ_CE(13, 14);
+  } else {
+    QZ_CE(0, 1); QZ_CE(2, 3); QZ_CE(0, 2); QZ_CE(1, 3); QZ_CE(1, 2); QZ_CE(4, 5);
+    QZ_CE(6, 7); QZ_CE(4, 6); QZ_CE(5, 7); QZ_CE(5, 6); QZ_CE(0, 4); QZ_CE(2, 6);
+    QZ_CE(2, 4); QZ_CE(1, 5); QZ_CE(3, 7); QZ_CE(3, 5); QZ_CE(1, 2); QZ_CE(3, 4);
+    QZ_CE(5, 6); QZ_CE(8, 9); QZ_CE(10, 11); QZ_CE(8, 10); QZ_CE(9, 11); QZ_CE(9, 10);
+    QZ_CE(12, 13); QZ_CE(14, 15); QZ_CE(12, 14); QZ_CE(13, 15); QZ_CE(13, 14); QZ_CE(8, 12);
+    QZ_CE(10, 14); QZ_CE(10, 12); QZ_CE(9, 13); QZ_CE(11, 15); QZ_CE(11, 13); QZ_CE(9, 10);
+    QZ_CE(11, 12); QZ_CE(13, 14); QZ_CE(0, 8); QZ_CE(4, 12); QZ_CE(4, 8); QZ_CE(2, 10);
+    QZ_CE(6, 14); QZ_CE(6, 10); QZ_CE(2, 4); QZ_CE(6, 8); QZ_CE(10, 12); QZ_CE(1, 9);
+    QZ_CE(5, 13); QZ_CE(5, 9); QZ_CE(3, 11); QZ_CE(7, 15); QZ_CE(7, 11); QZ_CE(3, 5);
+    QZ_CE(7, 9); QZ_CE(11, 13); QZ_CE(1, 2); QZ_CE(3, 4); QZ_CE(5, 6); QZ_CE(7, 8);
+    QZ_CE(9, 10); QZ_CE(11, 12); QZ_CE(13, 14); QZ_CE(16, 17); QZ_CE(18, 19); QZ_CE(16, 18);
+    QZ_CE(17, 19); QZ_CE(17, 18); QZ_CE(20, 21); QZ_CE(22, 23); QZ_CE(20, 22); QZ_CE(21, 23);
+    QZ_CE(21, 22); QZ_CE(16, 20); QZ_CE(18, 22); QZ_CE(18, 20); QZ_CE(17, 21); QZ_CE(19, 23);
+    QZ_CE(19, 21); QZ_CE(17, 18); QZ_CE(19, 20); QZ_CE(21, 22); QZ_CE(24, 25); QZ_CE(26, 27);
+    QZ_CE(24, 26); QZ_CE(25, 27); QZ_CE(25, 26); QZ_CE(28, 29); QZ_CE(30, 31); QZ_CE(28, 30);
+    QZ_CE(29, 31); QZ_CE(29, 30); QZ_CE(24, 28); QZ_CE(26, 30); QZ_CE(26, 28); QZ_CE(25, 29);
+    QZ_CE(27, 31); QZ_CE(27, 29); QZ_CE(25, 26); QZ_CE(27, 28); QZ_CE(29, 30); QZ_CE(16, 24);
+    QZ_CE(20, 28); QZ_CE(20, 24); QZ_CE(18, 26); QZ_CE(22, 30); QZ_CE(22, 26); QZ_CE(18, 20);
+    QZ_CE(22, 24); QZ_CE(26, 28); QZ_CE(17, 25); QZ_CE(21, 29); QZ_CE(21, 25); QZ_CE(19, 27);
+    QZ_CE(23, 31); QZ_CE(23, 27); QZ_CE(19, 21); QZ_CE(23, 25); QZ_CE(27, 29); QZ_CE(17, 18);
+    QZ_CE(19, 20); QZ_CE(21, 22); QZ_CE(23, 24); QZ_CE(25, 26); QZ_CE(27, 28); QZ_CE(29, 30);
+    QZ_CE(0, 16); QZ_CE(8, 24); QZ_CE(8, 16); QZ_CE(4, 20); QZ_CE(12, 28); QZ_CE(12, 20);
+    QZ_CE(4, 8); QZ_CE(12, 16); QZ_CE(20, 24); QZ_CE(2, 18); QZ_CE(10, 26); QZ_CE(10, 18);
+    QZ_CE(6, 22); QZ_CE(14, 30); QZ_CE(14, 22); QZ_CE(6, 10); QZ_CE(14, 18); QZ_CE(22, 26);
+    QZ_CE(2, 4); QZ_CE(6, 8); QZ_CE(10, 12); QZ_CE(14, 16); QZ_CE(18, 20); QZ_CE(22, 24);
+    QZ_CE(26, 28); QZ_CE(1, 17); QZ_CE(9, 25); QZ_CE(9, 17); QZ_CE(5, 21); QZ_CE(13, 29);
+    QZ_CE(13, 21); QZ_CE(5, 9); QZ_CE(13, 17); QZ_CE(21, 25); QZ_CE(3, 19); QZ_CE(11, 27);
+    QZ_CE(11, 19); QZ_CE(7, 23); QZ_CE(15, 31); QZ_CE(15, 23); QZ_CE(7, 11); QZ_CE(15, 19);
+    QZ_CE(23, 27); QZ_CE(3, 5); QZ_CE(7, 9); QZ_CE(11, 13); QZ_CE(15, 17); QZ_CE(19, 21);
+    QZ_CE(23, 25); QZ_CE(27, 29); QZ_CE(1, 2); QZ_CE(3, 4); QZ_CE(5, 6); QZ_CE(7, 8);
+    QZ_CE(9, 10); QZ_CE(11, 12); QZ_CE(13, 14); QZ_CE(15, 16); QZ_CE(17, 18); QZ_CE(19, 20);
+    QZ_CE(21, 22); QZ_CE(23, 24); QZ_CE(25, 26); QZ_CE(27, 28); QZ_CE(29, 30);
   }
 }
+#undef QZ_CE
 
 template <int DT>
 struct Elem { static constexpr int kSize = DT == kDtF32 ? 4 : 2; };

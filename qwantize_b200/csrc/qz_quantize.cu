@@ -173,6 +173,16 @@ __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable&
   else return block_sse<BS, MODE>(a, t.val[code]);
 }
 
+// SSE of the naive scale s0 (finite, >= 0): the hardware path when s0 > 0 and
+// the input is 16-bit; s0 = 0 (NVFP4 blocks below 6 * 2^-10) takes the generic one.
+template <int BS, int MODE, int DT, int FMT>
+__device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
+  if constexpr (DT != kDtF32) {
+    if (s > 0.0f) return block_sse_hw<BS>(a, s, __fmul_rn(__frcp_rn(s), kBiasDown));
+  }
+  return block_sse<BS, MODE>(a, s);
+}
+
 // Clipping error sum(clamp(|x| - 6 s, 0)^2) (nvfp4/reference.py:209).
 template <int BS>
 __device__ __forceinline__ float block_clip(const float (&a)[BS], float s) {
@@ -259,7 +269,7 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
   uint32_t srt[BS];
 #pragma unroll
   for (int i = 0; i < BS; ++i) srt[i] = __float_as_uint(a[i]);
-  bitonic_sort_u32<BS>(srt);
+  sort_u32<BS>(srt);
   double c = 0.0;
   int k_star = 0;
 #pragma unroll
@@ -544,7 +554,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
       // MXFP4: 1-4 power-of-two candidates per block; each lane walks its own
       // (the ascending loop with strict '<', clipping fast-fail omitted as above).
       if (valid && !s_nan) {
-        const float E0 = block_sse<BS, MODE>(a, s);
+        const float E0 = base_sse<BS, MODE, DT, FMT>(a, s);
         int lo, hi;
         search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
         float best_E = E0;
@@ -560,7 +570,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
       int lo = 1, hi = 0;
       float E0 = 0.0f;
       if (valid && !s_nan) {
-        E0 = block_sse<BS, MODE>(a, s);
+        E0 = base_sse<BS, MODE, DT, FMT>(a, s);
         search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
       }
       const int n = hi >= lo ? hi - lo + 1 : 0;
