@@ -239,6 +239,76 @@ __device__ __forceinline__ float block_hess(const float (&x)[BS], const float (&
   return res;
 }
 
+// Shared-memory float4 load the compiler may not hoist: H_j is loop-invariant
+// across candidates, and keeping all of it in registers (bs*bs floats) spills.
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+// r^T H r as block_hess computes it (each row of H r is a sequential FMA chain
+// over b ascending, then the torch sum order over a of r_a * (H r)_a), with the
+// rows' chains interleaved for instruction-level parallelism.  Ht is H_j
+// transposed in shared memory (Ht[b*BS + a] = H_j[a][b]), so one broadcast
+// float4 load feeds four chains.  For bf16/fp16 inputs and s > 0 the residual
+// uses the hardware rounding: r = x - sign(x) q s = +-RN(|x| - q s) with the
+// sign of x applied by flipping the sign bit, bit-identical to the generic path
+// (q s is exact).
+template <int BS, int MODE, int DT>
+__device__ __forceinline__ float block_hess_ilp(const float (&x)[BS], const float (&a)[BS], float s,
+                                                const float* __restrict__ Ht) {
+  float r[BS];
+  if (DT != kDtF32 && s > 0.0f) {
+    const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
+#pragma unroll
+    for (int i = 0; i < BS; i += 2) {
+      const float2 q = e2m1x2_to_float2(e2m1x2_rn(__fmul_rn(a[i], c), __fmul_rn(a[i + 1], c)));
+      // x - sign(x) q s = sign(x) * (|x| - q s): flip by x's sign bit (keeps -0.0)
+      r[i] = __uint_as_float(__float_as_uint(__fmaf_rn(-q.x, s, a[i])) ^ (__float_as_uint(x[i]) & 0x80000000u));
+      r[i + 1] = __uint_as_float(__float_as_uint(__fmaf_rn(-q.y, s, a[i + 1])) ^
+                                 (__float_as_uint(x[i + 1]) & 0x80000000u));
+    }
+  } else {
+    FastQ<MODE> q(s);
+#pragma unroll
+    for (int i = 0; i < BS; ++i) {
+      const float t = q(a[i]);
+      const float dq = x[i] > 0.0f ? t : (x[i] < 0.0f ? -t : 0.0f);
+      r[i] = __fsub_rn(x[i], dq);
+    }
+  }
+  float acc8[8];
+#pragma unroll
+  for (int g = 0; g < BS; g += 16) {
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
+#pragma unroll
+    for (int b = 0; b < BS; ++b) {
+      const uint32_t hrow = smem_u32(Ht + b * BS + g);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const float4 h = lds_f4(hrow + 16 * q4);
+        acc[4 * q4 + 0] = __fmaf_rn(h.x, r[b], acc[4 * q4 + 0]);
+        acc[4 * q4 + 1] = __fmaf_rn(h.y, r[b], acc[4 * q4 + 1]);
+        acc[4 * q4 + 2] = __fmaf_rn(h.z, r[b], acc[4 * q4 + 2]);
+        acc[4 * q4 + 3] = __fmaf_rn(h.w, r[b], acc[4 * q4 + 3]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int ai = g + k;
+      const float pa = __fmul_rn(r[ai], acc[k]);
+      acc8[ai & 7] = ai < 8 ? pa : __fadd_rn(acc8[ai & 7], pa);
+    }
+  }
+  float res = acc8[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) res = __fadd_rn(res, acc8[k]);
+  return res;
+}
+
 // Naive scale for FMT from amax bits (NaN propagates with the reference's bits).
 template <int FMT>
 __device__ __forceinline__ float naive_scale(uint32_t amax_bits) {
@@ -619,14 +689,16 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
   }
 }
 
-// Hessian method: CTA (j, row chunk); the CTA's H_j lives in shared memory.
+// Hessian method: CTA (j, row chunk); the CTA's H_j lives (transposed) in
+// shared memory.  Each thread walks its block's candidates in ascending order
+// with the reference's fast-fail rule, which does depend on the running best.
 template <int BS, int FMT, int DT>
 __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
   constexpr int MODE = Mode<FMT, DT>::v;
-  __shared__ __align__(16) float Hs[BS * BS];
+  __shared__ __align__(16) float Ht[BS * BS];
   const int64_t j = blockIdx.x;
   const float* Hg = p.h_blocks + j * (BS * BS);
-  for (int i = threadIdx.x; i < BS * BS; i += blockDim.x) Hs[i] = Hg[i];
+  for (int i = threadIdx.x; i < BS * BS; i += blockDim.x) Ht[(i % BS) * BS + i / BS] = Hg[i];
   __syncthreads();
   const int64_t M = p.n_blocks / p.n_col_blocks;
   for (int64_t m = (int64_t)blockIdx.y * blockDim.x + threadIdx.x; m < M;
@@ -637,19 +709,19 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
     uint32_t amax_bits = abs_and_amax<BS>(x, a);
     float s = naive_scale<FMT>(amax_bits);
     if (!is_nan_bits(__float_as_uint(s) & 0x7fffffffu)) {
-      float E0 = block_sse<BS, MODE>(a, s);
-      float best_E = block_hess<BS, MODE>(x, a, s, Hs);
+      const float E0 = base_sse<BS, MODE, DT, FMT>(a, s);
+      float best_E = block_hess_ilp<BS, MODE, DT>(x, a, s, Ht);
       int lo, hi;
       search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
 #pragma unroll 1
       for (int c = lo; c <= hi; ++c) {
-        float sc = cand_value<FMT>(c);
-        float Hc = block_clip<BS>(a, sc);
+        const float sc = cand_value<FMT>(c);
+        const float Hc = block_clip<BS>(a, sc);
         // NVFP4 fast-fail: 10x the running Hessian best (nvfp4/reference.py:377);
         // MXFP4: the baseline SSE (mxfp4/reference.py:346).
-        bool pass = FMT == kNVFP4 ? (Hc < __fmul_rn(best_E, 10.0f)) : (Hc < E0);
+        const bool pass = FMT == kNVFP4 ? (Hc < __fmul_rn(best_E, 10.0f)) : (Hc < E0);
         if (!pass) continue;
-        float E = block_hess<BS, MODE>(x, a, sc, Hs);
+        const float E = block_hess_ilp<BS, MODE, DT>(x, a, sc, Ht);
         if (E < best_E) { best_E = E; s = sc; }
       }
     }
