@@ -96,6 +96,54 @@ __device__ __forceinline__ float block_sse(const float (&a)[BS], float s) {
   return sum8<BS>(d2);
 }
 
+// Packed fp32 pairs (sm_100a f32x2 arithmetic): two independent IEEE
+// round-to-nearest operations per instruction, the same results as two scalar
+// __f*_rn operations.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 up2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// sum8 over squared pairs: acc lanes (k, k+1) are one packed pair, so the
+// element pair (i, i+1) with i even adds into pair (i % 8) / 2.
+template <int BS>
+__device__ __forceinline__ float sum8_pairs(const uint64_t (&sq)[BS / 2]) {
+  uint64_t acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = sq[k];
+#pragma unroll
+  for (int i = 4; i < BS / 2; ++i) acc[i & 3] = add2(acc[i & 3], sq[i]);
+  const float2 p0 = up2(acc[0]), p1 = up2(acc[1]), p2 = up2(acc[2]), p3 = up2(acc[3]);
+  float r = __fadd_rn(p0.x, p0.y);
+  r = __fadd_rn(r, p1.x);
+  r = __fadd_rn(r, p1.y);
+  r = __fadd_rn(r, p2.x);
+  r = __fadd_rn(r, p2.y);
+  r = __fadd_rn(r, p3.x);
+  return __fadd_rn(r, p3.y);
+}
+
 // Block SSE with hardware rounding: bf16/fp16 inputs, finite s > 0, with
 // c = RN(RN(1/s) * (1 - 2^-13)) precomputed.  d = a - q*s is one FMA: q*s is
 // exact in fp32 (q has <= 2 significant bits, s <= 4, and a UE8M0 product that
@@ -103,16 +151,17 @@ __device__ __forceinline__ float block_sse(const float (&a)[BS], float s) {
 // the reference's rounding of a - dq.
 template <int BS>
 __device__ __forceinline__ float block_sse_hw(const float (&a)[BS], float s, float c) {
-  float d2[BS];
+  uint64_t sq[BS / 2];
+  const uint64_t c2 = pk2(c, c), ms2 = pk2(-s, -s);
 #pragma unroll
   for (int i = 0; i < BS; i += 2) {
-    const float2 q = e2m1x2_to_float2(e2m1x2_rn(__fmul_rn(a[i], c), __fmul_rn(a[i + 1], c)));
-    const float d0 = __fmaf_rn(-q.x, s, a[i]);
-    const float d1 = __fmaf_rn(-q.y, s, a[i + 1]);
-    d2[i] = __fmul_rn(d0, d0);
-    d2[i + 1] = __fmul_rn(d1, d1);
+    const uint64_t a2 = pk2(a[i], a[i + 1]);
+    const float2 y = up2(mul2(a2, c2));
+    const float2 q = e2m1x2_to_float2(e2m1x2_rn(y.x, y.y));
+    const uint64_t d = fma2(pk2(q.x, q.y), ms2, a2);
+    sq[i / 2] = mul2(d, d);
   }
-  return sum8<BS>(d2);
+  return sum8_pairs<BS>(sq);
 }
 
 // NVFP4 variant: the decoded codes stay in f16 and feed a mixed-precision FMA
@@ -135,15 +184,17 @@ __device__ __forceinline__ uint32_t e2m1x2_to_half2_bits(uint32_t byte) {
 
 template <int BS>
 __device__ __forceinline__ float block_sse_hw_nv(const float (&a)[BS], uint32_t neg_s_h, float c) {
-  float d2[BS];
+  uint64_t sq[BS / 2];
+  const uint64_t c2 = pk2(c, c);
 #pragma unroll
   for (int i = 0; i < BS; i += 2) {
-    const uint32_t q = e2m1x2_to_half2_bits(e2m1x2_rn(__fmul_rn(a[i], c), __fmul_rn(a[i + 1], c)));
+    const float2 y = up2(mul2(pk2(a[i], a[i + 1]), c2));
+    const uint32_t q = e2m1x2_to_half2_bits(e2m1x2_rn(y.x, y.y));
     const float2 d = fma2_f16(q, neg_s_h, a[i], a[i + 1]);
-    d2[i] = __fmul_rn(d.x, d.x);
-    d2[i + 1] = __fmul_rn(d.y, d.y);
+    const uint64_t d2 = pk2(d.x, d.y);
+    sq[i / 2] = mul2(d2, d2);
   }
-  return sum8<BS>(d2);
+  return sum8_pairs<BS>(sq);
 }
 
 // Per-CTA table of candidate scales and their biased reciprocals, indexed by
@@ -553,7 +604,7 @@ struct WarpGeom {
 
 // Naive / SSE / argmin methods.
 template <int BS, int FMT, int METHOD, int DT>
-__global__ void __launch_bounds__(kThreads) quantize_kernel(QuantArgs p) {
+__global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT == kNVFP4 ? 4 : 1) : 2) : 1) quantize_kernel(QuantArgs p) {
   using G = WarpGeom<BS, FMT, DT, METHOD>;
   constexpr int MODE = Mode<FMT, DT>::v;
   constexpr int S = G::kStages;
