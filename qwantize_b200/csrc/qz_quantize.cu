@@ -381,10 +381,13 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
                                              float amax, float E0, int& lo, int& hi) {
   lo = 1;
   hi = 0;
-  float sq[BS];
+  uint64_t sq[BS / 2];  // x.pow(2).sum(-1), packed pairs (x*x == |x|*|x| bit for bit)
 #pragma unroll
-  for (int i = 0; i < BS; ++i) sq[i] = __fmul_rn(x[i], x[i]);
-  bool noise = sum8<BS>(sq) <= E0;
+  for (int i = 0; i < BS; i += 2) {
+    const uint64_t a2 = pk2(a[i], a[i + 1]);
+    sq[i / 2] = mul2(a2, a2);
+  }
+  bool noise = sum8_pairs<BS>(sq) <= E0;
   float s_min = __fdiv_rn(__fsub_rn(amax, __fsqrt_rn(E0)), 6.0f);
   s_min = s_min < 0.0f ? 0.0f : s_min;
   uint32_t srt[BS];
