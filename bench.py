@@ -417,12 +417,17 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         torch.distributed.all_reduce(Hbd)
     ms_nv = _ev_time(lambda: q.nvfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
     ms_mx = _ev_time(lambda: q.mxfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    from qwantize_b200.core import admm_fp32
+    from qwantize_b200.hessian import admm_setup
+    Hn, Minv = admm_setup(Hbd)
+    ms_admm = _ev_time(lambda: admm_fp32(Wb, -1, False, Hbd, Hn, Minv), stream, 3)
     _, _, dq = q.nvfp4_optimal(Wb, return_dequant=True)
     dqb = dq.reshape(2560, Kx).to(torch.bfloat16)
     ms_m = _max_over_ranks(_ev_time(lambda: output_error_sums(W, dqb, X), stream), ws, device)
     mflop = 4 * (t1 - t0) * Kx * 2560
     out["config2_hopt"] = {
         "weights": 2560 * Kx, "nvfp4_bs16_search_ms": ms_nv, "mxfp4_bs16_search_ms": ms_mx,
+        "nvfp4_admm_bs16_ms": ms_admm,
         "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
         "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9}
     del X, H

@@ -85,6 +85,20 @@ QZ_API int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_s
                 uint16_t* dq_bf16, void* stream);
 
 /*
+ * qz_admm -- ADMM refinement of NVFP4 codes and scales under block Hessians.
+ * Replaces the iteration of nvfp4_admm (nvfp4/reference.py:466-534): from the
+ * naive E4M3 scale, n_outer rounds of (n_inner ADMM steps projecting onto the
+ * E2M1 codebook, then s = E4M3(x^T H q / q^T H q)).  The caller supplies, per
+ * column block j, H_j, H_j / lambda_max(H_j) and inv(H_j / lambda_max + rho I)
+ * (each (n_col_blocks, bs, bs) fp32; block b uses j = b % n_col_blocks).
+ * quants / packed hold the ADMM codes; outputs as in qz_quantize.
+ */
+QZ_API int qz_admm(const void* x, int x_dtype, int64_t n_blocks, int block_size, const float* h_blocks,
+                   const float* hn_blocks, const float* minv_blocks, int64_t n_col_blocks, int n_outer,
+                   int n_inner, float rho, float* scales, float* quants, float* dq, uint8_t* scale_codes,
+                   uint8_t* packed, uint16_t* dq_bf16, void* stream);
+
+/*
  * qz_dequantize -- out = quants * scales per block.  Replaces nvfp4_dequantize
  * (nvfp4/reference.py:537-549) and mxfp4_dequantize (mxfp4/reference.py:377-389)
  * in the blocked layout.

@@ -175,3 +175,19 @@ def metrics_sums(W_bf16, Wdq, X_bf16=None):
     Xc = None if X_bf16 is None else np.ascontiguousarray(X_bf16, np.uint16)
     lib().qzo_metrics(W.ctypes.data, Wdq.ctypes.data, M, K, _ptr(Xc), T, out.ctypes.data)
     return out
+
+
+def admm(x_bf16, bs, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.0):
+    """nvfp4_admm's iteration given (J, bs, bs) H, H/lambda_max, M_inv."""
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1)
+    n_blocks = x.size // bs
+    H, Hn, Minv = (np.ascontiguousarray(t, np.float32) for t in (H, Hn, Minv))
+    J = H.shape[0]
+    L = lib()
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    L.qzo_admm.argtypes = [vp, i32, i64, i32, vp, vp, vp, i64, i32, i32, ctypes.c_float, vp, vp]
+    scales = np.empty(n_blocks, np.float32)
+    quants = np.empty(n_blocks * bs, np.float32)
+    L.qzo_admm(x.ctypes.data, DT_BF16, n_blocks, bs, H.ctypes.data, Hn.ctypes.data, Minv.ctypes.data, J,
+               n_outer, n_inner, rho, scales.ctypes.data, quants.ctypes.data)
+    return scales, quants

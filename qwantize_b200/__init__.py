@@ -10,7 +10,7 @@ from .metrics import compute_metrics
 from .mxfp4 import (mxfp4_dequantize, mxfp4_dequantize_packed, mxfp4_naive, mxfp4_naive_torch,
                     mxfp4_naive_triton, mxfp4_optimal, mxfp4_optimal_hessian, mxfp4_optimal_torch,
                     mxfp4_optimal_triton, mxfp4_quantize_packed)
-from .nvfp4 import (nvfp4_dequantize, nvfp4_dequantize_packed, nvfp4_naive, nvfp4_naive_triton,
+from .nvfp4 import (nvfp4_admm, nvfp4_dequantize, nvfp4_dequantize_packed, nvfp4_naive, nvfp4_naive_triton,
                     nvfp4_optimal, nvfp4_optimal_hessian, nvfp4_optimal_hessian_triton,
                     nvfp4_optimal_triton, nvfp4_quantize_packed)
 

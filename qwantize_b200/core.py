@@ -117,3 +117,27 @@ def dequantize_native(scale_codes, packed, fmt, dtype=torch.bfloat16):
     L.check(L.load().qz_dequantize_packed(L.ptr(p), L.ptr(c), n_blocks, bs, fmt, L.ptr(f32),
                                           L.ptr(b16), L.stream_ptr(dev)), "qz_dequantize_packed")
     return out.to(packed.device)
+
+
+def admm_fp32(W, dim, return_dequant, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.0):
+    """nvfp4_admm's iteration (qz_admm) on blocks of W given the per-column-block
+    H, H / lambda_max and inv(H / lambda_max + rho I)."""
+    dim, bs, batch_shape, x, dev = _blocks(W, dim)
+    N = x.shape[0]
+    J = H.shape[0]
+    M_dim = N // J if J else 0
+    assert N == M_dim * J, f"Weight blocks ({N}) must equal M * K//bs ({M_dim} * {J})"
+    scales = torch.empty(N, dtype=torch.float32, device=dev)
+    quants = torch.empty(N, bs, dtype=torch.float32, device=dev)
+    dq = torch.empty(N, bs, dtype=torch.float32, device=dev) if return_dequant else None
+    H, Hn, Minv = (t.to(dev, torch.float32).contiguous() for t in (H, Hn, Minv))
+    st = L.load().qz_admm(L.ptr(x), L.dtype_code(x.dtype), N, bs, L.ptr(H), L.ptr(Hn), L.ptr(Minv), J,
+                          int(n_outer), int(n_inner), float(rho), L.ptr(scales), L.ptr(quants), L.ptr(dq),
+                          None, None, None, L.stream_ptr(dev))
+    L.check(st, "qz_admm")
+    out_dev = W.device
+    res = (scales.reshape(*batch_shape).to(out_dev),
+           quants.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev))
+    if return_dequant:
+        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev),)
+    return res

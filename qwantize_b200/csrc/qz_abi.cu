@@ -127,6 +127,31 @@ int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, in
                      "qz_quantize launch");
 }
 
+int qz_admm(const void* x, int x_dtype, int64_t n_blocks, int block_size, const float* h_blocks,
+            const float* hn_blocks, const float* minv_blocks, int64_t n_col_blocks, int n_outer, int n_inner,
+            float rho, float* scales, float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,
+            uint16_t* dq_bf16, void* stream) {
+  if (block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (x_dtype != QZ_DTYPE_F32 && x_dtype != QZ_DTYPE_BF16 && x_dtype != QZ_DTYPE_F16)
+    return fail(QZ_ERR_INVALID, "unknown dtype %d", x_dtype);
+  if (n_blocks < 0 || n_outer < 0 || n_inner < 0) return fail(QZ_ERR_INVALID, "negative size or iteration count");
+  if (n_blocks == 0) return QZ_OK;
+  if (!x || !h_blocks || !hn_blocks || !minv_blocks) return fail(QZ_ERR_INVALID, "NULL input");
+  if (n_col_blocks <= 0 || n_blocks % n_col_blocks != 0 || n_col_blocks > 2147483647LL)
+    return fail(QZ_ERR_INVALID, "n_blocks (%lld) must be a multiple of n_col_blocks (%lld)", (long long)n_blocks,
+                (long long)n_col_blocks);
+  if (!aligned(x, 16) || (quants && !aligned(quants, 16)) || (dq && !aligned(dq, 16)))
+    return fail(QZ_ERR_INVALID, "x, quants and dq must be 16-byte aligned");
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  QuantArgs p{x, n_blocks, h_blocks, n_col_blocks, scales, quants, dq, scale_codes, packed, dq_bf16};
+  return cuda_status(launch_admm(p, h_blocks, hn_blocks, minv_blocks, n_outer, n_inner, rho, x_dtype, block_size,
+                                 sms, static_cast<cudaStream_t>(stream)),
+                     "qz_admm launch");
+}
+
 int qz_dequantize(const float* scales, const float* quants, int64_t n_blocks, int block_size,
                   float* out, void* stream) {
   if (block_size != 16 && block_size != 32)

@@ -21,6 +21,8 @@ struct QuantArgs {
 
 cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int method,
                             int num_sms, cudaStream_t st);
+cudaError_t launch_admm(const QuantArgs& qa, const float* h, const float* hn, const float* minv, int n_outer,
+                        int n_inner, float rho, int dtype, int bs, int num_sms, cudaStream_t st);
 cudaError_t launch_dequantize(const float* scales, const float* quants, int64_t n_blocks, int bs,
                               float* out, int num_sms, cudaStream_t st);
 cudaError_t launch_dequantize_packed(const uint8_t* packed, const uint8_t* codes, int64_t n_blocks,

@@ -784,6 +784,166 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
 }
 
 // ---------------------------------------------------------------------------
+// ADMM refinement (nvfp4/reference.py:410-534): one thread per block, CTA per
+// column block j with H_j, H_j / lambda_max and inv(H_j / lambda_max + rho I)
+// transposed in shared memory.  The reference stops all blocks once no scale
+// changed; a block whose scale did not change reproduces itself exactly on
+// another pass, so each block stops on its own (same results).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float quant_unit(float v) {  // fp4_quantize(v, 1)
+  const float a = fabsf(v);
+  int idx = 0;
+#pragma unroll
+  for (int k = 0; k < 7; ++k) idx += (a <= bnd(k)) ? 0 : 1;
+  const float q = cb_rt((uint32_t)idx);
+  return v > 0.0f ? q : (v < 0.0f ? -q : 0.0f);
+}
+
+// y = A v with A^T in shared memory (At[b*BS + a] = A[a][b]); every y[a] is a
+// sequential FMA chain over b ascending.
+template <int BS>
+__device__ __forceinline__ void matvec_t(const float* __restrict__ At, const float (&v)[BS], float (&y)[BS]) {
+#pragma unroll
+  for (int k = 0; k < BS; ++k) y[k] = 0.0f;
+#pragma unroll
+  for (int b = 0; b < BS; ++b) {
+    const uint32_t row = smem_u32(At + b * BS);
+#pragma unroll
+    for (int q4 = 0; q4 < BS / 4; ++q4) {
+      const float4 h = lds_f4(row + 16 * q4);
+      y[4 * q4 + 0] = __fmaf_rn(h.x, v[b], y[4 * q4 + 0]);
+      y[4 * q4 + 1] = __fmaf_rn(h.y, v[b], y[4 * q4 + 1]);
+      y[4 * q4 + 2] = __fmaf_rn(h.z, v[b], y[4 * q4 + 2]);
+      y[4 * q4 + 3] = __fmaf_rn(h.w, v[b], y[4 * q4 + 3]);
+    }
+  }
+}
+
+struct AdmmArgs {
+  QuantArgs q;
+  const float* h;     // (J, bs, bs)
+  const float* hn;    // (J, bs, bs)
+  const float* minv;  // (J, bs, bs)
+  int n_outer, n_inner;
+  float rho;
+};
+
+template <int BS, int DT>
+__global__ void __launch_bounds__(64) admm_kernel(AdmmArgs A) {
+  const QuantArgs& p = A.q;
+  __shared__ __align__(16) float Ht[BS * BS], Hnt[BS * BS], Mt[BS * BS];
+  const int64_t j = blockIdx.x;
+  for (int i = threadIdx.x; i < BS * BS; i += blockDim.x) {
+    const int t = (i % BS) * BS + i / BS;
+    Ht[t] = A.h[j * BS * BS + i];
+    Hnt[t] = A.hn[j * BS * BS + i];
+    Mt[t] = A.minv[j * BS * BS + i];
+  }
+  __syncthreads();
+  const int64_t M = p.n_blocks / p.n_col_blocks;
+  for (int64_t m = (int64_t)blockIdx.y * blockDim.x + threadIdx.x; m < M; m += (int64_t)gridDim.y * blockDim.x) {
+    const int64_t b = m * p.n_col_blocks + j;
+    float x[BS], a[BS];
+    load_block<BS, DT>(p.x, b, x);
+    const uint32_t amax_bits = abs_and_amax<BS>(x, a);
+    float s = naive_scale<kNVFP4>(amax_bits);
+    float z[BS], u[BS], hw[BS], v[BS];
+#pragma unroll
+    for (int i = 0; i < BS; ++i) z[i] = 0.0f;
+#pragma unroll 1
+    for (int t = 0; t < A.n_outer; ++t) {
+#pragma unroll
+      for (int i = 0; i < BS; ++i) {
+        v[i] = __fdiv_rn(x[i], s);  // w = x / s
+        z[i] = quant_unit(v[i]);
+        u[i] = 0.0f;
+      }
+      matvec_t<BS>(Hnt, v, hw);  // Hw = H_norm w
+#pragma unroll 1
+      for (int k = 0; k < A.n_inner; ++k) {
+#pragma unroll
+        for (int i = 0; i < BS; ++i) v[i] = __fadd_rn(hw[i], __fmul_rn(A.rho, __fsub_rn(z[i], u[i])));
+        float q[BS];
+        matvec_t<BS>(Mt, v, q);  // q = M_inv rhs
+#pragma unroll
+        for (int i = 0; i < BS; ++i) {
+          z[i] = quant_unit(__fadd_rn(q[i], u[i]));
+          u[i] = __fsub_rn(__fadd_rn(u[i], q[i]), z[i]);
+        }
+      }
+      // scale update: s = E4M3(x^T H q* / q*^T H q*) where valid
+      matvec_t<BS>(Ht, z, v);  // Hq
+      float pn[BS], pd[BS];
+#pragma unroll
+      for (int i = 0; i < BS; ++i) {
+        pn[i] = __fmul_rn(x[i], v[i]);
+        pd[i] = __fmul_rn(z[i], v[i]);
+      }
+      const float numer = sum8<BS>(pn), denom = sum8<BS>(pd);
+      const bool valid = numer > 0.0f && denom > 1e-12f;
+      float sc = __fdiv_rn(numer, denom < 1e-12f ? 1e-12f : denom);
+      sc = sc < 1e-12f ? 1e-12f : sc;
+      const float s_new = valid ? e4m3_snap_nonneg(sc) : s;
+      if (s_new == s) break;
+      s = s_new;
+    }
+    // outputs: quants are the ADMM codes z (not a re-quantization of x)
+    const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
+    if (p.scales) p.scales[b] = s;
+    if (p.scale_codes) p.scale_codes[b] = (uint8_t)e4m3_code(s);
+    float dq[BS];
+    uint32_t nib[BS];
+#pragma unroll
+    for (int i = 0; i < BS; ++i) {
+      dq[i] = snan ? s : __fmul_rn(z[i], s);
+      const uint32_t zb = __float_as_uint(z[i]), mag = zb & 0x7fffffffu;
+      const uint32_t idx = mag == 0u ? 0u : (mag == 0x3f000000u ? 1u : ((mag - 0x3f000000u) >> 22));
+      nib[i] = ((zb >> 31) << 3) | idx;
+    }
+    if (p.quants) {
+      float4* o = reinterpret_cast<float4*>(p.quants + b * BS);
+#pragma unroll
+      for (int k = 0; k < BS / 4; ++k) o[k] = make_float4(z[4 * k], z[4 * k + 1], z[4 * k + 2], z[4 * k + 3]);
+    }
+    if (p.dq) {
+      float4* o = reinterpret_cast<float4*>(p.dq + b * BS);
+#pragma unroll
+      for (int k = 0; k < BS / 4; ++k) o[k] = make_float4(dq[4 * k], dq[4 * k + 1], dq[4 * k + 2], dq[4 * k + 3]);
+    }
+    if (p.dq_bf16) {
+#pragma unroll
+      for (int i = 0; i < BS; ++i) p.dq_bf16[b * BS + i] = (uint16_t)(__float_as_uint(dq[i]) >> 16);
+    }
+    if (p.packed) {
+#pragma unroll
+      for (int i = 0; i < BS; i += 2) p.packed[b * (BS / 2) + i / 2] = (uint8_t)(nib[i] | (nib[i + 1] << 4));
+    }
+  }
+}
+
+cudaError_t launch_admm(const QuantArgs& qa, const float* h, const float* hn, const float* minv, int n_outer,
+                        int n_inner, float rho, int dtype, int bs, int num_sms, cudaStream_t st) {
+  if (qa.n_blocks == 0) return cudaSuccess;
+  AdmmArgs A{qa, h, hn, minv, n_outer, n_inner, rho};
+  const int64_t M = qa.n_blocks / qa.n_col_blocks;
+  int64_t gy = (M + 63) / 64;
+  const int64_t per_j = ((int64_t)num_sms * 16 + qa.n_col_blocks - 1) / qa.n_col_blocks;
+  gy = gy < per_j ? gy : per_j;
+  gy = gy < 1 ? 1 : (gy > 65535 ? 65535 : gy);
+  dim3 grid((unsigned)qa.n_col_blocks, (unsigned)gy);
+  if (bs == 16) {
+    if (dtype == kDtBF16) admm_kernel<16, kDtBF16><<<grid, 64, 0, st>>>(A);
+    else if (dtype == kDtF16) admm_kernel<16, kDtF16><<<grid, 64, 0, st>>>(A);
+    else admm_kernel<16, kDtF32><<<grid, 64, 0, st>>>(A);
+  } else {
+    if (dtype == kDtBF16) admm_kernel<32, kDtBF16><<<grid, 64, 0, st>>>(A);
+    else if (dtype == kDtF16) admm_kernel<32, kDtF16><<<grid, 64, 0, st>>>(A);
+    else admm_kernel<32, kDtF32><<<grid, 64, 0, st>>>(A);
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // host-side launch
 // ---------------------------------------------------------------------------
 template <int BS, int FMT, int METHOD, int DT>

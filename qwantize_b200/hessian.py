@@ -47,3 +47,16 @@ def resolve_h_blocks(W: torch.Tensor, dim: int, X, H_blocks) -> torch.Tensor:
     if H_blocks is not None:
         return H_blocks.to(dev, torch.float32).contiguous()
     return block_hessians(X, bs)
+
+
+def admm_setup(H: torch.Tensor, rho: float = 1.0):
+    """The per-column-block matrices of nvfp4_admm (nvfp4/reference.py:466-475):
+    H_norm = H / max(lambda_max(H), 1e-6) and M_inv = inv(H_norm + rho I), from
+    batched bs x bs symmetric eigenvalue and inverse routines on the device."""
+    bs = H.shape[-1]
+    ev = torch.linalg.eigvalsh(H)
+    max_eig = ev[:, -1].clamp(min=1e-6)
+    Hn = H / max_eig.reshape(-1, 1, 1)
+    eye = torch.eye(bs, device=H.device, dtype=H.dtype).unsqueeze(0)
+    Minv = torch.linalg.inv(Hn + rho * eye)
+    return Hn.contiguous(), Minv.contiguous()

@@ -18,7 +18,7 @@ from ..reference_helpers import (D_0, FP4_BOUNDARIES, FP4_CODEBOOK, Q_MAX, compu
                                  fp4_dequantize, fp4_quantize)
 
 __all__ = [
-    "nvfp4_naive", "nvfp4_optimal", "nvfp4_optimal_hessian", "nvfp4_dequantize",
+    "nvfp4_naive", "nvfp4_optimal", "nvfp4_optimal_hessian", "nvfp4_admm", "nvfp4_dequantize",
     "nvfp4_naive_triton", "nvfp4_optimal_triton", "nvfp4_optimal_hessian_triton",
     "nvfp4_quantize_packed", "nvfp4_dequantize_packed", "build_fp8_e4m3_scales",
     "fp4_quantize", "fp4_dequantize", "compute_block_sse",
@@ -47,6 +47,28 @@ def nvfp4_optimal_hessian(W, dim=-1, return_dequant=False, X=None, H_blocks=None
     H_j = X_j^T X_j is built on the tensor cores when only X is given."""
     H = _h(W, dim, X, H_blocks)
     return _q(W, dim, return_dequant, L.FMT_NVFP4, L.METHOD_HESSIAN, H)
+
+
+def nvfp4_admm(W, dim=-1, return_dequant=False, X=None, n_outer=3, n_inner=10, H_blocks=None):
+    """ADMM-refined NVFP4 quantization under the block Hessians of X
+    (nvfp4/reference.py:410-534): from the naive scale, n_outer rounds of
+    n_inner ADMM steps that project onto the E2M1 codebook, then a closed-form
+    E4M3 scale update.  H_j = X_j^T X_j is built on the tensor cores
+    (``H_blocks`` may be passed instead, an extension of the reference's
+    signature); the iteration runs in the qz_admm kernel."""
+    assert X is not None or H_blocks is not None, "X (activations) required for ADMM quantization"
+    from ..core import admm_fp32
+    from ..hessian import admm_setup, block_hessians
+    dim_ = dim % W.ndim
+    bs = W.shape[dim_]
+    assert bs in (16, 32)
+    if H_blocks is None:
+        H = block_hessians(X, bs)
+    else:
+        from ..core import cuda_device
+        H = H_blocks.to(cuda_device(W), torch.float32).contiguous()
+    Hn, Minv = admm_setup(H, 1.0)
+    return admm_fp32(W, dim, return_dequant, H, Hn, Minv, n_outer, n_inner, 1.0)
 
 
 def nvfp4_dequantize(scales, quants, dim=-1):

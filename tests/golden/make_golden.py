@@ -160,6 +160,8 @@ def main(ref_root: str, skip_digests: bool = False):
         hout[f"mx_H_{bs}_scales"], hout[f"mx_H_{bs}_quants"] = s.numpy(), qq.numpy()
         s, qq, dq = mx_hess(Wb, return_dequant=True, X=X)
         hout[f"mx_X_{bs}_scales"] = s.numpy()
+        s, qq, dq = q.nvfp4_admm(Wb, return_dequant=True, X=X)
+        hout[f"admm_X_{bs}_scales"], hout[f"admm_X_{bs}_quants"] = s.numpy(), qq.numpy()
     np.savez_compressed(os.path.join(HERE, "hessian_small.npz"), **hout)
 
     # ---- metrics fixture ----------------------------------------------------
