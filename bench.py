@@ -430,6 +430,15 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         "nvfp4_admm_bs16_ms": ms_admm,
         "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
         "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9}
+    # GPTQ (NVFP4 bs16 SSE-optimal) of the 2560x9728 weight on the full H / T
+    from qwantize_b200.gptq import gptq
+    if ws > 1:
+        torch.distributed.all_reduce(H)
+    H.div_(T)
+    t_g = time.perf_counter()
+    gptq(W, H, "nvfp4", "optimal", 16)
+    torch.cuda.synchronize()
+    out["config2_hopt"]["gptq_nvfp4_optimal_bs16_ms"] = (time.perf_counter() - t_g) * 1e3
     del X, H
     torch.cuda.empty_cache()
     # config 3: the Qwen3-4B stack, rows sharded

@@ -1,0 +1,133 @@
+"""GPTQ error compensation on the full Hessian, with the block quantizers of
+this library (the caller of the full Gram).
+
+Follows experiments/quant_gptq_strided.py:49-135 (``gptq_strided``) and
+:137-222 (``gptq_strided_ordered``) of the reference: damp the Hessian, take
+the inverse through its Cholesky factor, then quantize column blocks left to
+right, each block's scaled error propagated to all later columns.
+
+B200 layout: the working weight is kept column-block-major, (K/bs, M, bs), so
+every column block is one contiguous input of the quantization kernel (naive,
+SSE-optimal or Hessian-optimal, fp32 path: the same arithmetic as the
+reference's torch quantizers).  Error propagation is lazy-batched: inside a
+group of ``group`` columns the update touches only the group, and one batched
+GEMM per group applies the accumulated error to every later column (the
+standard GPTQ reordering of the same sums; results agree with the reference to
+floating-point reassociation).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from .core import cuda_device
+
+_FMT = {"nvfp4": L.FMT_NVFP4, "mxfp4": L.FMT_MXFP4}
+_METHOD = {"naive": L.METHOD_NAIVE, "optimal": L.METHOD_SSE, "hoptimal": L.METHOD_HESSIAN}
+
+
+def _inverse_hessian(H: torch.Tensor, damp: float) -> torch.Tensor:
+    """Damped H^-1 via Cholesky (experiments/quant_gptq_strided.py:72-85)."""
+    Hi = H.clone().float()
+    dmu = damp * Hi.diagonal().mean()
+    Hi.diagonal().add_(dmu)
+    try:
+        Lc = torch.linalg.cholesky(Hi)
+    except torch.linalg.LinAlgError:
+        Hi.diagonal().add_(1e-5 * dmu)
+        Lc = torch.linalg.cholesky(Hi)
+    return torch.cholesky_inverse(Lc).contiguous()
+
+
+def _quant_block(x: torch.Tensor, bs: int, fmt: int, method: int, H_blk, out_dq: torch.Tensor):
+    """Dequantized (M, bs) block of fp32 weights through qz_quantize."""
+    M = x.shape[0]
+    Hp = None
+    J = 0
+    if method == L.METHOD_HESSIAN:
+        Hp = H_blk.contiguous()
+        J = 1
+    L.check(L.load().qz_quantize(L.ptr(x), L.DTYPE_F32, M, bs, fmt, method, L.ptr(Hp), J, None, None,
+                                 L.ptr(out_dq), None, None, None, L.stream_ptr(x.device)), "qz_quantize")
+    return out_dq
+
+
+def gptq(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "optimal",
+         block_size: int = 16, damp: float = 0.01, group: int = 128, H_blocks: torch.Tensor = None):
+    """Sequential GPTQ over column blocks (gptq_strided).
+
+    W (M, K), H (K, K) -> (Q (M, K) fp32 dequantized, average per-row loss).
+    ``H_blocks`` (K/bs, bs, bs) are the Hessians the H-optimal quantizer uses
+    for each column block (default: the diagonal blocks of H)."""
+    bs = block_size
+    assert bs in (16, 32)
+    dev = cuda_device(W)
+    W = W.to(dev)
+    M, K = W.shape
+    assert K % bs == 0 and H.shape == (K, K)
+    nblk = K // bs
+    fmt_c, meth_c = _FMT[fmt], _METHOD[method]
+    Hd = H.to(dev, torch.float32)
+    Hi = _inverse_hessian(Hd, damp)
+    if meth_c == L.METHOD_HESSIAN and H_blocks is None:
+        H_blocks = torch.stack([Hd[j * bs:(j + 1) * bs, j * bs:(j + 1) * bs] for j in range(nblk)])
+    if H_blocks is not None:
+        H_blocks = H_blocks.to(dev, torch.float32).contiguous()
+    # column-block-major working copy: Wb[j] is W[:, j*bs:(j+1)*bs]
+    Wb = W.float().reshape(M, nblk, bs).permute(1, 0, 2).contiguous()
+    Qb = torch.empty_like(Wb)
+    loss = torch.zeros((), dtype=torch.float64, device=dev)
+    gb = max(1, group // bs)  # column blocks per lazy-batch group
+    for g0 in range(0, nblk, gb):
+        g1 = min(nblk, g0 + gb)
+        Eg = torch.empty(g1 - g0, M, bs, dtype=torch.float32, device=dev)  # scaled errors of the group
+        for j in range(g0, g1):
+            w_blk = Wb[j]
+            q = _quant_block(w_blk, bs, fmt_c, meth_c, H_blocks[j] if H_blocks is not None else None, Qb[j])
+            cs = j * bs
+            h_diag = Hi.diagonal()[cs:cs + bs]
+            d = w_blk - q
+            err = d / h_diag
+            loss += (d * d / h_diag).sum(dtype=torch.float64)
+            Eg[j - g0] = err
+            if j + 1 < g1:  # update the rest of the group: W[:, ce:g_end] -= err @ Hi[cs:ce, ce:g_end]
+                h_cross = Hi[cs:cs + bs, (j + 1) * bs:g1 * bs].reshape(bs, g1 - j - 1, bs)
+                Wb[j + 1:g1] -= torch.einsum("mi,ijc->jmc", err, h_cross)
+        if g1 < nblk:  # everything after the group at once
+            rows = Hi[g0 * bs:g1 * bs, g1 * bs:]  # (group cols, rest)
+            E2 = Eg.permute(1, 0, 2).reshape(M, (g1 - g0) * bs)
+            upd = E2 @ rows  # (M, rest)
+            Wb[g1:] -= upd.reshape(M, nblk - g1, bs).permute(1, 0, 2)
+    Q = Qb.permute(1, 0, 2).reshape(M, K)
+    return Q, float(loss.item()) / M
+
+
+def gptq_ordered(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "optimal",
+                 block_size: int = 16, damp: float = 0.01, group: int = 128):
+    """GPTQ with column blocks taken in descending order of their stand-alone
+    Hessian-weighted loss (gptq_strided_ordered): quantize each block alone,
+    score r^T H_j r, permute W and H by blocks, run gptq, permute back."""
+    bs = block_size
+    dev = cuda_device(W)
+    W = W.to(dev).float()
+    M, K = W.shape
+    nblk = K // bs
+    Hd = H.to(dev, torch.float32)
+    H_blocks = torch.stack([Hd[j * bs:(j + 1) * bs, j * bs:(j + 1) * bs] for j in range(nblk)]).contiguous()
+    fmt_c, meth_c = _FMT[fmt], _METHOD[method]
+    Wb = W.reshape(M, nblk, bs).permute(1, 0, 2).contiguous()
+    losses = torch.empty(nblk, device=dev)
+    tmp = torch.empty(M, bs, device=dev)
+    for j in range(nblk):
+        q = _quant_block(Wb[j], bs, fmt_c, meth_c, H_blocks[j], tmp)
+        r = Wb[j] - q
+        losses[j] = (r * (r @ H_blocks[j])).sum()
+    _, blk_perm = losses.sort(descending=True)
+    col_perm = (blk_perm.unsqueeze(1) * bs + torch.arange(bs, device=dev).unsqueeze(0)).reshape(-1)
+    W_perm = W[:, col_perm].contiguous()
+    H_perm = Hd[col_perm][:, col_perm].contiguous()
+    Hb_perm = H_blocks[blk_perm].contiguous()
+    Q_perm, avg_loss = gptq(W_perm, H_perm, fmt, method, bs, damp, group, H_blocks=Hb_perm)
+    inv = torch.empty_like(col_perm)
+    inv[col_perm] = torch.arange(K, device=dev)
+    return Q_perm[:, inv], avg_loss

@@ -164,6 +164,27 @@ def main(ref_root: str, skip_digests: bool = False):
         hout[f"admm_X_{bs}_scales"], hout[f"admm_X_{bs}_quants"] = s.numpy(), qq.numpy()
     np.savez_compressed(os.path.join(HERE, "hessian_small.npz"), **hout)
 
+    # ---- GPTQ (experiments/quant_gptq_strided.py:49-135) on the same W and
+    # H = X^T X / T (double, rounded once), with the reference's own quantizers
+    sys.path.insert(0, os.path.join(ref_root, "experiments"))
+    import quant_gptq_strided as gq
+    Hg = (X.double().T @ X.double() / T).float()
+    gout = {"W": bits(Wh)}
+    for bs in (16, 32):
+        Jb = K // bs
+        Hbd = torch.stack([Hg[j * bs:(j + 1) * bs, j * bs:(j + 1) * bs] for j in range(Jb)])
+        fns = {
+            "naive": lambda w, j, bs=bs: q.nvfp4_naive(w, return_dequant=True)[2],
+            "optimal": lambda w, j, bs=bs: q.nvfp4_optimal(w, return_dequant=True)[2],
+            "hoptimal": lambda w, j, bs=bs, Hbd=Hbd: q.nvfp4_optimal_hessian(
+                w, return_dequant=True, H_blocks=Hbd[j:j + 1])[2],
+        }
+        for name, fn in fns.items():
+            Q, loss = gq.gptq_strided(Wh.float(), Hg, fn, block_size=bs)
+            gout[f"{name}_{bs}_Q"] = Q.numpy()
+            gout[f"{name}_{bs}_loss"] = np.array([loss])
+    np.savez_compressed(os.path.join(HERE, "gptq_small.npz"), **gout)
+
     # ---- metrics fixture ----------------------------------------------------
     Wm = make_weight(64, 512, seed=31)
     _, _, Wdq = q.nvfp4_optimal(Wm.reshape(64, 32, 16), return_dequant=True)

@@ -1,0 +1,54 @@
+"""GPTQ on the full Hessian (experiments/quant_gptq_strided.py) with this
+library's quantization kernels, against the reference's gptq_strided run with
+its own quantizers on the same W and H = X^T X / T.  Error propagation
+reassociates fp32 sums (lazy-batched groups, batched GEMMs; still a code that
+flips early changes every later column's input, so the bar is statistical:
+the GPTQ loss within 0.5% and >= 97% of dequantized weights identical."""
+import numpy as np
+import pytest
+import torch
+
+from tests._golden import load
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _inputs():
+    from qwantize_b200.synthetic import make_activations
+    g = load("hessian_small.npz")
+    X = make_activations(int(g["T"]), int(g["K"]), seed=int(g["x_seed"]), chunk_tokens=int(g["x_chunk"]))
+    H = (X.double().T @ X.double() / X.shape[0]).float()
+    W = torch.from_numpy(g["W"].view(np.int16)).view(torch.bfloat16)
+    return W, H
+
+
+@pytest.mark.parametrize("bs", [16, 32])
+@pytest.mark.parametrize("method", ["naive", "optimal", "hoptimal"])
+def test_gptq_vs_reference(method, bs):
+    from qwantize_b200.gptq import gptq
+    W, H = _inputs()
+    gg = load("gptq_small.npz")
+    Q, loss = gptq(W.to(DEV), H.to(DEV), "nvfp4", method, bs)
+    Qr = gg[f"{method}_{bs}_Q"]
+    ref_loss = float(gg[f"{method}_{bs}_loss"][0])
+    same = (Q.cpu().numpy() == Qr).mean()
+    print(method, bs, "identical", same, "loss", loss, ref_loss)
+    assert abs(loss - ref_loss) <= 1e-5 * ref_loss
+    assert same >= 0.999
+
+
+def test_gptq_ordered_runs_and_beats_naive_quantization():
+    import qwantize_b200 as q
+    from qwantize_b200.gptq import gptq_ordered
+    W, H = _inputs()
+    Wd = W.to(DEV)
+    Q, loss = gptq_ordered(Wd, H.to(DEV), "nvfp4", "optimal", 16)
+    # output-space error tr(E H E^T) below plain SSE-optimal quantization
+    _, _, dq = q.nvfp4_optimal(Wd.reshape(W.shape[0], -1, 16), return_dequant=True)
+    Hd = H.to(DEV)
+
+    def out_err(Qm):
+        E = Qm.float() - Wd.float()
+        return float((E @ Hd * E).sum())
+    assert out_err(Q) < out_err(dq.reshape(W.shape))
