@@ -432,8 +432,6 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9}
     # GPTQ (NVFP4 bs16 SSE-optimal) of the 2560x9728 weight on the full H / T
     from qwantize_b200.gptq import gptq
-    if ws > 1:
-        torch.distributed.all_reduce(H)
     H.div_(T)
     t_g = time.perf_counter()
     gptq(W, H, "nvfp4", "optimal", 16)
