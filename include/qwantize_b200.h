@@ -85,6 +85,20 @@ QZ_API int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_s
                 uint16_t* dq_bf16, void* stream);
 
 /*
+ * qz_quantize_table -- qz_quantize with a caller-supplied scale grid: `table`
+ * is a device array of n_table (2..256) ascending positive fp32 scales, e.g.
+ * the unsigned 8-bit UE4M4 / UE5M3 grids of exotic_scales.py:17-57.  Follows
+ * the exotic-grid experiment (experiments/quant_exotic_scales.py:48-182): the
+ * naive scale is snap_to_table(max|x| / 6) (exotic_scales.py:60-74), the
+ * searches run over the table with the NVFP4 rules.  scale_codes receive the
+ * table index.  Methods: naive, SSE, Hessian.
+ */
+QZ_API int qz_quantize_table(const void* x, int x_dtype, int64_t n_blocks, int block_size, int method,
+                             const float* table, int n_table, const float* h_blocks, int64_t n_col_blocks,
+                             float* scales, float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,
+                             uint16_t* dq_bf16, void* stream);
+
+/*
  * qz_admm -- ADMM refinement of NVFP4 codes and scales under block Hessians.
  * Replaces the iteration of nvfp4_admm (nvfp4/reference.py:466-534): from the
  * naive E4M3 scale, n_outer rounds of (n_inner ADMM steps projecting onto the

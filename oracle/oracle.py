@@ -191,3 +191,25 @@ def admm(x_bf16, bs, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.0):
     L.qzo_admm(x.ctypes.data, DT_BF16, n_blocks, bs, H.ctypes.data, Hn.ctypes.data, Minv.ctypes.data, J,
                n_outer, n_inner, rho, scales.ctypes.data, quants.ctypes.data)
     return scales, quants
+
+
+def quantize_table(x, bs, method, table, H=None, bf16=True):
+    """qzo_quantize with a caller-supplied ascending scale table."""
+    x = np.ascontiguousarray(x).reshape(-1)
+    n_blocks = x.size // bs
+    dt = _dtype_code(x, bf16)
+    t = np.ascontiguousarray(table, np.float32)
+    scales = np.empty(n_blocks, np.float32)
+    quants = np.empty(n_blocks * bs, np.float32)
+    dq = np.empty(n_blocks * bs, np.float32)
+    J = 0
+    if method == M_HESSIAN:
+        H = np.ascontiguousarray(H, np.float32)
+        J = H.shape[0]
+    L = lib()
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    L.qzo_quantize_table.argtypes = [vp, i32, i64, i32, i32, vp, i32, vp, i64, vp, vp, vp]
+    L.qzo_quantize_table.restype = i64
+    L.qzo_quantize_table(x.ctypes.data, dt, n_blocks, bs, method, t.ctypes.data, t.size, _ptr(H), J,
+                         scales.ctypes.data, quants.ctypes.data, dq.ctypes.data)
+    return scales, quants, dq

@@ -25,6 +25,7 @@ EXPORTS = [
     "qz_quantize", "qz_dequantize", "qz_dequantize_packed", "qz_fp4_unpack", "qz_gram",
     "qz_weight_error_sums", "qz_output_error_sums", "qz_scale_table", "qz_last_error",
     "qz_version", "qz_device_ok", "qz_poll_device_error", "qz_gram_full_noalloc", "qz_admm",
+    "qz_quantize_table",
 ]
 
 _lib = None
@@ -45,6 +46,7 @@ def load():
     vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
     L.qz_quantize.argtypes = [vp, i32, i64, i32, i32, i32, vp, i64, vp, vp, vp, vp, vp, vp, vp]
     L.qz_dequantize.argtypes = [vp, vp, i64, i32, vp, vp]
+    L.qz_quantize_table.argtypes = [vp, i32, i64, i32, i32, vp, i32, vp, i64, vp, vp, vp, vp, vp, vp, vp]
     L.qz_admm.argtypes = [vp, i32, i64, i32, vp, vp, vp, i64, i32, i32, ctypes.c_float, vp, vp, vp, vp, vp,
                           vp, vp]
     L.qz_dequantize_packed.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp]

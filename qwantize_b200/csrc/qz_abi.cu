@@ -101,6 +101,8 @@ int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, in
     return fail(QZ_ERR_INVALID, "unknown format %d", format);
   if (method < QZ_METHOD_NAIVE || method > QZ_METHOD_TWO_ARGMIN)
     return fail(QZ_ERR_INVALID, "unknown method %d", method);
+  if (method >= QZ_METHOD_NAIVE_ARGMIN && format != QZ_FMT_MXFP4)
+    return fail(QZ_ERR_INVALID, "the argmin methods (mxfp4_*_torch) are MXFP4 only");
   if (x_dtype != QZ_DTYPE_F32 && x_dtype != QZ_DTYPE_BF16 && x_dtype != QZ_DTYPE_F16)
     return fail(QZ_ERR_INVALID, "unknown dtype %d", x_dtype);
   if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
@@ -150,6 +152,38 @@ int qz_admm(const void* x, int x_dtype, int64_t n_blocks, int block_size, const 
   return cuda_status(launch_admm(p, h_blocks, hn_blocks, minv_blocks, n_outer, n_inner, rho, x_dtype, block_size,
                                  sms, static_cast<cudaStream_t>(stream)),
                      "qz_admm launch");
+}
+
+int qz_quantize_table(const void* x, int x_dtype, int64_t n_blocks, int block_size, int method,
+                      const float* table, int n_table, const float* h_blocks, int64_t n_col_blocks,
+                      float* scales, float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,
+                      uint16_t* dq_bf16, void* stream) {
+  if (block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (method != QZ_METHOD_NAIVE && method != QZ_METHOD_SSE && method != QZ_METHOD_HESSIAN)
+    return fail(QZ_ERR_INVALID, "table formats support the naive, SSE and Hessian methods, got %d", method);
+  if (x_dtype != QZ_DTYPE_F32 && x_dtype != QZ_DTYPE_BF16 && x_dtype != QZ_DTYPE_F16)
+    return fail(QZ_ERR_INVALID, "unknown dtype %d", x_dtype);
+  if (!table || n_table < 2 || n_table > 256)
+    return fail(QZ_ERR_INVALID, "table must hold 2..256 sorted positive scales, got %d", n_table);
+  if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
+  if (n_blocks == 0) return QZ_OK;
+  if (!x || !aligned(x, 16)) return fail(QZ_ERR_INVALID, "x must be non-NULL and 16-byte aligned");
+  if ((quants && !aligned(quants, 16)) || (dq && !aligned(dq, 16)) || (dq_bf16 && !aligned(dq_bf16, 16)) ||
+      (packed && !aligned(packed, block_size == 16 ? 8 : 16)))
+    return fail(QZ_ERR_INVALID, "quants/dq/dq_bf16 must be 16-byte aligned, packed 8/16-byte aligned");
+  if (method == QZ_METHOD_HESSIAN) {
+    if (!h_blocks) return fail(QZ_ERR_INVALID, "X or H_blocks required");
+    if (n_col_blocks <= 0 || n_blocks % n_col_blocks != 0 || n_col_blocks > 2147483647LL)
+      return fail(QZ_ERR_INVALID, "n_blocks (%lld) must be a multiple of n_col_blocks (%lld)",
+                  (long long)n_blocks, (long long)n_col_blocks);
+  }
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  QuantArgs p{x, n_blocks, h_blocks, n_col_blocks, scales, quants, dq, scale_codes, packed, dq_bf16, table, n_table};
+  return cuda_status(launch_quantize_table(p, x_dtype, block_size, method, sms, static_cast<cudaStream_t>(stream)),
+                     "qz_quantize_table launch");
 }
 
 int qz_dequantize(const float* scales, const float* quants, int64_t n_blocks, int block_size,

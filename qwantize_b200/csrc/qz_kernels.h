@@ -17,8 +17,11 @@ struct QuantArgs {
   uint8_t* scale_codes;
   uint8_t* packed;
   uint16_t* dq_bf16;
+  const float* table;  // kTable format: sorted positive scale values (device), n_table of them
+  int n_table;
 };
 
+cudaError_t launch_quantize_table(const QuantArgs& p, int dtype, int bs, int method, int num_sms, cudaStream_t st);
 cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int method,
                             int num_sms, cudaStream_t st);
 cudaError_t launch_admm(const QuantArgs& qa, const float* h, const float* hn, const float* minv, int n_outer,

@@ -40,7 +40,7 @@ namespace qz {
 //   MXFP4: |x| times the exact reciprocal 2^-e (identical to the quotient).
 enum RoundMode { kCmp = 0, kDiv = 1, kRcp = 2 };
 template <int FMT, int DT>
-struct Mode { static constexpr int v = FMT == kMXFP4 ? kRcp : (DT == kDtF32 ? kDiv : kCmp); };
+struct Mode { static constexpr int v = FMT == kMXFP4 ? kRcp : ((DT == kDtF32 || FMT == kTable) ? kDiv : kCmp); };
 
 // Dequant magnitude t = q*s for a = |x| and a finite scale s >= 0.
 template <int MODE>
@@ -203,10 +203,29 @@ struct CandTable {
   float val[256];
   float c[256];
   uint32_t neg_h[256];  // f16 bits of -val (NVFP4)
+  float mid[256];       // kTable: midpoints (t[i] + t[i+1]) * 0.5 of snap_to_table
+  int n;                // number of candidate codes (kTable: table length)
 };
 
+// One per CTA of every kernel that uses it (file-scope shared variable).
+__shared__ CandTable s_ctab;
+
 template <int FMT>
-__device__ __forceinline__ void fill_cand_table(CandTable& t) {
+__device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table = nullptr, int n_table = 0) {
+  if constexpr (FMT == kTable) {
+    // exotic_scales.py:60-74 snap_to_table: nearest entry via bucketize over
+    // midpoints computed in fp32; the candidates are the table itself
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+      const float v = i < n_table ? table[i] : 1.0f;
+      t.val[i] = v;
+      t.c[i] = 0.0f;
+      t.neg_h[i] = 0u;
+      t.mid[i] = i + 1 < n_table ? __fmul_rn(__fadd_rn(table[i], table[i + 1]), 0.5f) : 0.0f;
+    }
+    if (threadIdx.x == 0) t.n = n_table;
+    return;
+  }
+  if (threadIdx.x == 0) t.n = FMT == kNVFP4 ? 127 : 255;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
     const bool ok = FMT == kNVFP4 ? (i >= 1 && i <= 126) : (i >= 1 && i <= 254);
     const float v = ok ? (FMT == kNVFP4 ? e4m3_value(i) : pow2f(i - 127)) : 1.0f;
@@ -220,7 +239,7 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t) {
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
   if constexpr (DT != kDtF32 && FMT == kNVFP4) return block_sse_hw_nv<BS>(a, t.neg_h[code], t.c[code]);
-  else if constexpr (DT != kDtF32) return block_sse_hw<BS>(a, t.val[code], t.c[code]);
+  else if constexpr (DT != kDtF32 && FMT == kMXFP4) return block_sse_hw<BS>(a, t.val[code], t.c[code]);
   else return block_sse<BS, MODE>(a, t.val[code]);
 }
 
@@ -228,7 +247,7 @@ __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable&
 // the input is 16-bit; s0 = 0 (NVFP4 blocks below 6 * 2^-10) takes the generic one.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
-  if constexpr (DT != kDtF32) {
+  if constexpr (DT != kDtF32 && FMT != kTable) {
     if (s > 0.0f) return block_sse_hw<BS>(a, s, __fmul_rn(__frcp_rn(s), kBiasDown));
   }
   return block_sse<BS, MODE>(a, s);
@@ -310,7 +329,7 @@ template <int BS, int MODE, int DT>
 __device__ __forceinline__ float block_hess_ilp(const float (&x)[BS], const float (&a)[BS], float s,
                                                 const float* __restrict__ Ht) {
   float r[BS];
-  if (DT != kDtF32 && s > 0.0f) {
+  if (MODE != kDiv && s > 0.0f) {  // 16-bit input with an E4M3 / UE8M0 scale
     const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
 #pragma unroll
     for (int i = 0; i < BS; i += 2) {
@@ -360,9 +379,33 @@ __device__ __forceinline__ float block_hess_ilp(const float (&x)[BS], const floa
   return res;
 }
 
+// Number of table entries below v (strict) / at or below v; v not NaN.
+__device__ __forceinline__ int table_count_below(float v, bool inclusive) {
+  int lo = 0, hi = s_ctab.n;
+  while (lo < hi) {
+    const int m = (lo + hi) >> 1;
+    const float t = s_ctab.val[m];
+    if (inclusive ? (t <= v) : (t < v)) lo = m + 1; else hi = m;
+  }
+  return lo;
+}
+
 // Naive scale for FMT from amax bits (NaN propagates with the reference's bits).
 template <int FMT>
 __device__ __forceinline__ float naive_scale(uint32_t amax_bits) {
+  if constexpr (FMT == kTable) {
+    // snap_to_table((amax / 6).clamp(min=1e-12)) (exotic_scales.py:60-74):
+    // bucketize over the midpoints (right=False; NaN -> last entry)
+    float c = __fdiv_rn(__uint_as_float(amax_bits), 6.0f);
+    c = c < 1e-12f ? 1e-12f : c;
+    int lo = 0, hi = s_ctab.n - 1;
+    if (is_nan_bits(amax_bits)) lo = hi;
+    while (lo < hi) {
+      const int m = (lo + hi) >> 1;
+      if (s_ctab.mid[m] < c) lo = m + 1; else hi = m;
+    }
+    return s_ctab.val[lo];
+  }
   if (is_nan_bits(amax_bits)) return __uint_as_float(FMT == kNVFP4 ? kNvNanBits : kMxNanBits);
   float amax = __uint_as_float(amax_bits);
   if (FMT == kNVFP4) {
@@ -409,7 +452,10 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
   for (int i = 0; i < BS; ++i) y = (i == kidx) ? __uint_as_float(srt[i]) : y;
   float s_max = __fdiv_rn(y, 0.25f);
   if (noise || !(s_min <= s_max)) return;
-  if (FMT == kNVFP4) {
+  if (FMT == kTable) {
+    lo = table_count_below(s_min, false);
+    hi = table_count_below(s_max, true) - 1;
+  } else if (FMT == kNVFP4) {
     lo = e4m3_ceil_code(s_min);
     hi = e4m3_floor_code(s_max);
   } else {
@@ -423,6 +469,7 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
 
 template <int FMT>
 __device__ __forceinline__ float cand_value(int c) {
+  if constexpr (FMT == kTable) return s_ctab.val[c];
   return FMT == kNVFP4 ? e4m3_value(c) : pow2f(c - 127);
 }
 
@@ -473,7 +520,7 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
   const uint32_t sb = __float_as_uint(s);
   // hardware rounding: 16-bit input, finite s > 0, no NaN element (a NaN
   // element makes amax, hence s, NaN)
-  if (!argmin && DT != kDtF32 && sb > 0u && sb < 0x7f800000u) {
+  if (!argmin && DT != kDtF32 && FMT != kTable && sb > 0u && sb < 0x7f800000u) {
     const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
 #pragma unroll
     for (int i = 0; i < BS; i += 2) {
@@ -505,7 +552,8 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
   const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
   if (p.scales) p.scales[b] = s;
   if (p.scale_codes) {
-    uint32_t code = FMT == kNVFP4 ? e4m3_code(s) : (snan ? 0xffu : (__float_as_uint(s) >> 23));
+    uint32_t code = FMT == kTable ? (uint32_t)table_count_below(s, false)
+                    : (FMT == kNVFP4 ? e4m3_code(s) : (snan ? 0xffu : (__float_as_uint(s) >> 23)));
     p.scale_codes[b] = (uint8_t)code;
   }
   float dq[BS];
@@ -598,7 +646,7 @@ template <int BS, int FMT, int DT, int METHOD>
 struct WarpGeom {
   static constexpr int kChunkBytes = 32 * BS * Elem<DT>::kSize;  // 1-4 KB
   static constexpr int kStages = kChunkBytes <= 2048 ? 4 : 2;
-  static constexpr bool kCoop = METHOD == kSSE && FMT == kNVFP4;
+  static constexpr bool kCoop = METHOD == kSSE && FMT != kMXFP4;
   static constexpr int kRowBytes = kCoop ? 32 * BS * 4 : 0;     // |x| rows for cooperation
   static constexpr int kBytes = kStages * kChunkBytes + kRowBytes + (kCoop ? 32 * 8 + 64 * 4 : 0) +
                                 kStages * 8;
@@ -612,10 +660,10 @@ __global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT ==
   constexpr int MODE = Mode<FMT, DT>::v;
   constexpr int S = G::kStages;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ CandTable ctab;
+  CandTable& ctab = s_ctab;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (METHOD == kSSE) {
-    fill_cand_table<FMT>(ctab);
+  if (METHOD == kSSE || FMT == kTable) {
+    fill_cand_table<FMT>(ctab, p.table, p.n_table);
     __syncthreads();
   }
   unsigned char* wbase = smem_raw + warp * G::kBytesAligned;
@@ -753,6 +801,7 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
   const int64_t j = blockIdx.x;
   const float* Hg = p.h_blocks + j * (BS * BS);
   for (int i = threadIdx.x; i < BS * BS; i += blockDim.x) Ht[(i % BS) * BS + i / BS] = Hg[i];
+  if (FMT == kTable) fill_cand_table<FMT>(s_ctab, p.table, p.n_table);
   __syncthreads();
   const int64_t M = p.n_blocks / p.n_col_blocks;
   for (int64_t m = (int64_t)blockIdx.y * blockDim.x + threadIdx.x; m < M;
@@ -773,7 +822,8 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
         const float Hc = block_clip<BS>(a, sc);
         // NVFP4 fast-fail: 10x the running Hessian best (nvfp4/reference.py:377);
         // MXFP4: the baseline SSE (mxfp4/reference.py:346).
-        const bool pass = FMT == kNVFP4 ? (Hc < __fmul_rn(best_E, 10.0f)) : (Hc < E0);
+        // (the exotic-grid experiment uses the NVFP4 rule: quant_exotic_scales.py:157)
+        const bool pass = FMT != kMXFP4 ? (Hc < __fmul_rn(best_E, 10.0f)) : (Hc < E0);
         if (!pass) continue;
         const float E = block_hess_ilp<BS, MODE, DT>(x, a, sc, Ht);
         if (E < best_E) { best_E = E; s = sc; }
@@ -983,8 +1033,12 @@ static cudaError_t launch_fmt_dt(const QuantArgs& p, int method, int num_sms, cu
   switch (method) {
     case kNaive: return launch_q<BS, FMT, kNaive, DT>(p, num_sms, st);
     case kSSE: return launch_q<BS, FMT, kSSE, DT>(p, num_sms, st);
-    case kNaiveArgmin: return launch_q<BS, FMT, kNaiveArgmin, DT>(p, num_sms, st);
-    case kTwoArgmin: return launch_q<BS, FMT, kTwoArgmin, DT>(p, num_sms, st);
+    case kNaiveArgmin:
+      if constexpr (FMT == kMXFP4) return launch_q<BS, FMT, kNaiveArgmin, DT>(p, num_sms, st);
+      return cudaErrorInvalidValue;
+    case kTwoArgmin:
+      if constexpr (FMT == kMXFP4) return launch_q<BS, FMT, kTwoArgmin, DT>(p, num_sms, st);
+      return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
@@ -996,6 +1050,13 @@ static cudaError_t launch_fmt(const QuantArgs& p, int dtype, int method, int sms
     case kDtF16: return launch_fmt_dt<BS, FMT, kDtF16>(p, method, sms, st);
     default: return launch_fmt_dt<BS, FMT, kDtF32>(p, method, sms, st);
   }
+}
+
+cudaError_t launch_quantize_table(const QuantArgs& p, int dtype, int bs, int method, int num_sms,
+                                  cudaStream_t st) {
+  if (p.n_blocks == 0) return cudaSuccess;
+  return bs == 16 ? launch_fmt<16, kTable>(p, dtype, method, num_sms, st)
+                  : launch_fmt<32, kTable>(p, dtype, method, num_sms, st);
 }
 
 cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int method,

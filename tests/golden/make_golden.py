@@ -185,6 +185,20 @@ def main(ref_root: str, skip_digests: bool = False):
             gout[f"{name}_{bs}_loss"] = np.array([loss])
     np.savez_compressed(os.path.join(HERE, "gptq_small.npz"), **gout)
 
+    # ---- exotic scale grids (experiments/quant_exotic_scales.py:48-182) ------
+    import quant_exotic_scales as qe
+    from qwantize.exotic_scales import build_ue4m4_scales, build_ue5m3_scales, snap_to_table
+    xout = {"W": bits(Wh), "E": bits(E)}
+    for tname, table in (("ue4m4", build_ue4m4_scales()), ("ue5m3", build_ue5m3_scales())):
+        xout[f"table_{tname}"] = table.numpy()
+        snap = (lambda v, t=table: snap_to_table(v, t))
+        for bs in (16, 32):
+            xout[f"{tname}_{bs}_naive"] = qe.fp4_naive(Wh, snap, bs).numpy()
+            xout[f"{tname}_{bs}_optimal"] = qe.fp4_optimal(Wh, table, snap, bs).numpy()
+            xout[f"{tname}_{bs}_hoptimal"] = qe.fp4_hoptimal(Wh, X, table, snap, bs).numpy()
+            xout[f"E_{tname}_{bs}_optimal"] = qe.fp4_optimal(E, table, snap, bs).numpy()
+    np.savez_compressed(os.path.join(HERE, "exotic_small.npz"), **xout)
+
     # ---- metrics fixture ----------------------------------------------------
     Wm = make_weight(64, 512, seed=31)
     _, _, Wdq = q.nvfp4_optimal(Wm.reshape(64, 32, 16), return_dequant=True)

@@ -1,0 +1,53 @@
+"""Exotic 8-bit scale grids (UE4M4, UE5M3; experiments/quant_exotic_scales.py)
+through qz_quantize_table: naive and SSE bit-exact against the reference
+experiment's outputs, Hessian-optimal bit-exact against the oracle given the
+same H and >= 99.9% against the reference (its H is built by fp32 addmm)."""
+import numpy as np
+import pytest
+import torch
+
+from tests._golden import load, n_diff_bits, same_bits
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _bf(u16):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("bs", [16, 32])
+@pytest.mark.parametrize("tname", ["ue4m4", "ue5m3"])
+def test_exotic_naive_optimal_bit_exact(tname, bs):
+    from qwantize_b200 import exotic
+    g = load("exotic_small.npz")
+    t = torch.from_numpy(g[f"table_{tname}"])
+    W = _bf(g["W"]).to(DEV)
+    for name, fn in (("naive", exotic.fp4_naive), ("optimal", exotic.fp4_optimal)):
+        dq = fn(W, t, bs).cpu().numpy()
+        assert same_bits(dq, g[f"{tname}_{bs}_{name}"]), (name, n_diff_bits(dq, g[f"{tname}_{bs}_{name}"]))
+    dqE = exotic.fp4_optimal(_bf(g["E"]).to(DEV), t, bs).cpu().numpy()
+    assert same_bits(dqE, g[f"E_{tname}_{bs}_optimal"])
+
+
+@pytest.mark.parametrize("bs", [16, 32])
+@pytest.mark.parametrize("tname", ["ue4m4", "ue5m3"])
+def test_exotic_hoptimal(oracle, tname, bs):
+    from qwantize_b200 import exotic
+    from qwantize_b200.synthetic import make_activations
+    from tests._golden import ref_admm_matrices
+    g = load("exotic_small.npz")
+    h = load("hessian_small.npz")
+    t = torch.from_numpy(g[f"table_{tname}"])
+    W = _bf(g["W"]).to(DEV)
+    M, K = W.shape
+    X = make_activations(int(h["T"]), K, seed=int(h["x_seed"]), chunk_tokens=int(h["x_chunk"]))
+    H = ref_admm_matrices(X, bs)[0]
+    s, qq, dq = exotic.quantize_table(W.reshape(M, K // bs, bs), t, "hoptimal", return_dequant=True, H_blocks=H)
+    os_, oq, odq = oracle.quantize_table(g["W"], bs, 2, g[f"table_{tname}"], H=H.numpy())
+    assert same_bits(s.cpu().numpy(), os_) and same_bits(dq.cpu().numpy(), odq)
+    ref = g[f"{tname}_{bs}_hoptimal"].reshape(-1)
+    same = (dq.cpu().numpy().reshape(-1) == ref).mean()
+    assert same >= 0.999, same
+    dq2 = exotic.fp4_hoptimal(W, X.to(DEV), t, bs)
+    assert (dq2.cpu().numpy().reshape(-1) == ref).mean() >= 0.999
