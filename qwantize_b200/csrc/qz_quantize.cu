@@ -647,6 +647,7 @@ struct WarpGeom {
   static constexpr int kChunkBytes = 32 * BS * Elem<DT>::kSize;  // 1-4 KB
   static constexpr int kStages = kChunkBytes <= 2048 ? 4 : 2;
   static constexpr bool kCoop = METHOD == kSSE && FMT != kMXFP4;
+  static constexpr int kCpi = 2;  // candidate codes per cooperative work item
   static constexpr int kRowBytes = kCoop ? 32 * BS * 4 : 0;     // |x| rows for cooperation
   static constexpr int kBytes = kStages * kChunkBytes + kRowBytes + (kCoop ? 32 * 8 + 64 * 4 : 0) +
                                 kStages * 8;
@@ -745,18 +746,23 @@ __global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT ==
         E0 = base_sse<BS, MODE, DT, FMT>(a, s);
         search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
       }
+      // Work items of CPI consecutive codes of one block: the lookup, the row
+      // reload and the atomic are paid once per item (the last item of a
+      // block repeats its highest code, which cannot change the minimum).
+      constexpr int CPI = G::kCpi;
       const int n = hi >= lo ? hi - lo + 1 : 0;
+      const int n_items = (n + CPI - 1) / CPI;
       float4* row = reinterpret_cast<float4*>(rows + lane * BS);
 #pragma unroll
       for (int v = 0; v < BS / 4; ++v) row[v] = make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
-      int sc = n;
+      int sc = n_items;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         int t = __shfl_up_sync(0xffffffffu, sc, o);
         if (lane >= o) sc += t;
       }
       incl[lane] = sc;
-      lo_s[lane] = lo;
+      lo_s[lane] = lo | (hi << 16);
       best[lane] = (unsigned long long)__float_as_uint(E0) << 32;
       const int total = __shfl_sync(0xffffffffu, sc, 31);
       __syncwarp();
@@ -764,7 +770,9 @@ __global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT ==
 #pragma unroll 1
       for (int it = lane; it < total; it += 32) {
         while (it >= incl[bb]) ++bb;
-        const int c = lo_s[bb] + (it - (bb ? incl[bb - 1] : 0));
+        const int lh = lo_s[bb];
+        const int c0 = (lh & 0xffff) + CPI * (it - (bb ? incl[bb - 1] : 0));
+        const int ch = lh >> 16;
         float ar[BS];
         const float4* r4 = reinterpret_cast<const float4*>(rows + bb * BS);
 #pragma unroll
@@ -772,12 +780,20 @@ __global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT ==
           float4 t = r4[v];
           ar[4 * v] = t.x; ar[4 * v + 1] = t.y; ar[4 * v + 2] = t.z; ar[4 * v + 3] = t.w;
         }
-        const float E = cand_sse<BS, MODE, DT, FMT>(ar, ctab, c);
-        atomicMin(best + bb, ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)c);
+        unsigned long long key = ~0ull;
+#pragma unroll
+        for (int k = 0; k < CPI; ++k) {
+          const int c = c0 + k <= ch ? c0 + k : ch;
+          const float E = cand_sse<BS, MODE, DT, FMT>(ar, ctab, c);
+          // low word c + 1: 0 stays the naive scale, which wins ties
+          const unsigned long long kk = ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)(c + 1);
+          key = kk < key ? kk : key;
+        }
+        atomicMin(best + bb, key);
       }
       __syncwarp();
       const unsigned win = (unsigned)(best[lane] & 0xffffffffu);
-      if (win != 0) s = ctab.val[win];
+      if (win != 0) s = ctab.val[win - 1];
       __syncwarp();  // rows/best are rewritten by the next chunk
     } else if constexpr (METHOD == kTwoArgmin) {
       if (valid && !s_nan) {

@@ -51,3 +51,24 @@ def test_exotic_hoptimal(oracle, tname, bs):
     assert same >= 0.999, same
     dq2 = exotic.fp4_hoptimal(W, X.to(DEV), t, bs)
     assert (dq2.cpu().numpy().reshape(-1) == ref).mean() >= 0.999
+
+
+@pytest.mark.parametrize("bs", [16, 32])
+def test_table_first_entry_wins(oracle, bs):
+    """A coarse table whose smallest entry is often the SSE-best scale while
+    the naive snap picks the next one: index 0 must be selectable."""
+    from qwantize_b200 import exotic
+    t = np.array([0.01, 0.011, 0.05, 0.2], np.float32)
+    g = torch.Generator().manual_seed(11)
+    M, K = 64, 256
+    mag = torch.exp(torch.empty(M, K // bs, 1).uniform_(np.log(0.02), np.log(0.1), generator=g))
+    W = (torch.randn(M, K // bs, bs, generator=g) * mag).reshape(M, K).to(torch.bfloat16)
+    u16 = W.view(torch.int16).numpy().view(np.uint16)
+    s, qq, dq = exotic.quantize_table(W.to(DEV).reshape(M, K // bs, bs), torch.from_numpy(t), "optimal",
+                                      return_dequant=True)
+    os_, oq, odq = oracle.quantize_table(u16, bs, 1, t)
+    s = s.cpu().numpy().reshape(-1)
+    assert same_bits(s, os_) and same_bits(dq.cpu().numpy().reshape(-1), odq.reshape(-1))
+    naive = exotic.quantize_table(W.to(DEV).reshape(M, K // bs, bs), torch.from_numpy(t), "naive")[0]
+    first = (s == t[0]) & (naive.cpu().numpy().reshape(-1) != t[0])
+    assert first.sum() > 0  # the case under test occurs
