@@ -511,6 +511,99 @@ __device__ __forceinline__ float block_sse_argmin(const float (&x)[BS], float s)
 }
 
 // Final quantization with scale s (any value, NaN included) and all outputs.
+
+// Eight signed E2M1 codes of y[0..7] (hardware RN, saturating), element k in
+// nibble k of the result (the packed storage order).
+__device__ __forceinline__ uint32_t e2m1x8_rn(const float (&y)[8]) {
+  uint32_t w;
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+      " mov.b32 %0, {b0, b1, b2, b3};\n}\n"
+      : "=r"(w)
+      : "f"(y[0]), "f"(y[1]), "f"(y[2]), "f"(y[3]), "f"(y[4]), "f"(y[5]), "f"(y[6]), "f"(y[7]));
+  return w;
+}
+
+// Byte k of w (two codes) decoded to f16x2 bits (exact, signs kept).
+template <int K>
+__device__ __forceinline__ uint32_t e2m1x2_byte_to_h2(uint32_t w) {
+  uint32_t h2;
+  asm("{\n .reg .b8 b;\n .reg .b32 t;\n shr.b32 t, %1, %2;\n cvt.u8.u32 b, t;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b;\n}\n"
+      : "=r"(h2) : "r"(w), "n"(8 * K));
+  return h2;
+}
+
+// q * s for both halves of a decoded f16x2 pair, s given as f16 bits (exact:
+// E2M1 x E4M3 products have <= 6 significant bits and lie in [2^-10, 2688]);
+// the -0 addend keeps the sign of a zero product (-0 * s = -0, as in torch).
+__device__ __forceinline__ float2 h2_times_s(uint32_t q_h2, uint32_t s_h) {
+  float d0, d1;
+  asm("{\n .reg .b16 lo, hi, s;\n mov.b32 {lo, hi}, %2;\n cvt.u16.u32 s, %3;\n"
+      " fma.rn.f32.f16 %0, lo, s, 0f80000000;\n fma.rn.f32.f16 %1, hi, s, 0f80000000;\n}\n"
+      : "=f"(d0), "=f"(d1) : "r"(q_h2), "r"(s_h));
+  return make_float2(d0, d1);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {  // exact inputs
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Outputs of one block from its packed codes (hardware path: finite s > 0).
+template <int BS, int FMT>
+__device__ __forceinline__ void write_outputs_hw(const QuantArgs& p, int64_t b, const uint32_t (&codes)[BS / 8],
+                                                 float s) {
+  if (p.scales) p.scales[b] = s;
+  if (p.scale_codes) p.scale_codes[b] = (uint8_t)(FMT == kNVFP4 ? e4m3_code(s) : (__float_as_uint(s) >> 23));
+  if (p.packed) {
+    if constexpr (BS == 16) *reinterpret_cast<uint2*>(p.packed + b * 8) = make_uint2(codes[0], codes[1]);
+    else *reinterpret_cast<uint4*>(p.packed + b * 16) = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+  }
+  const uint32_t s_h = FMT == kNVFP4 ? (uint32_t)__half_as_ushort(__float2half_rn(s)) : 0u;
+#pragma unroll
+  for (int w = 0; w < BS / 8; ++w) {  // eight elements per step, stored as they are made
+    float dq[8], q[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t h2;
+      if (k == 0) h2 = e2m1x2_byte_to_h2<0>(codes[w]);
+      else if (k == 1) h2 = e2m1x2_byte_to_h2<1>(codes[w]);
+      else if (k == 2) h2 = e2m1x2_byte_to_h2<2>(codes[w]);
+      else h2 = e2m1x2_byte_to_h2<3>(codes[w]);
+      if (p.quants || FMT != kNVFP4) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+        q[2 * k] = f.x;
+        q[2 * k + 1] = f.y;
+      }
+      if constexpr (FMT == kNVFP4) {
+        const float2 d = h2_times_s(h2, s_h);
+        dq[2 * k] = d.x;
+        dq[2 * k + 1] = d.y;
+      } else {
+        dq[2 * k] = __fmul_rn(q[2 * k], s);
+        dq[2 * k + 1] = __fmul_rn(q[2 * k + 1], s);
+      }
+    }
+    if (p.dq_bf16)
+      reinterpret_cast<uint4*>(p.dq_bf16 + b * BS)[w] =
+          make_uint4(pack_bf16x2(dq[0], dq[1]), pack_bf16x2(dq[2], dq[3]), pack_bf16x2(dq[4], dq[5]),
+                     pack_bf16x2(dq[6], dq[7]));
+    if (p.quants) {
+      float4* o = reinterpret_cast<float4*>(p.quants + b * BS + 8 * w);
+      o[0] = make_float4(q[0], q[1], q[2], q[3]);
+      o[1] = make_float4(q[4], q[5], q[6], q[7]);
+    }
+    if (p.dq) {
+      float4* o = reinterpret_cast<float4*>(p.dq + b * BS + 8 * w);
+      o[0] = make_float4(dq[0], dq[1], dq[2], dq[3]);
+      o[1] = make_float4(dq[4], dq[5], dq[6], dq[7]);
+    }
+  }
+}
+
 template <int BS, int FMT, int METHOD, int DT>
 __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const float (&x)[BS], float s) {
   constexpr int MODE = Mode<FMT, DT>::v;
@@ -521,20 +614,26 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
   // hardware rounding: 16-bit input, finite s > 0, no NaN element (a NaN
   // element makes amax, hence s, NaN)
   if (!argmin && DT != kDtF32 && FMT != kTable && sb > 0u && sb < 0x7f800000u) {
+    // Packed path: y = RN(x * c) + 0 makes -0 quantize to +0 (torch.sign(-0)
+    // is 0) while a negative value that rounds to zero keeps code 8 (-0), the
+    // reference's sign * 0; the hardware conversion gives sign and magnitude.
     const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
+    const uint64_t c2 = pk2(c, c), z2 = pk2(0.0f, 0.0f);
+    uint32_t codes[BS / 8];
 #pragma unroll
-    for (int i = 0; i < BS; i += 2) {
-      uint32_t byte = e2m1x2_rn(__fmul_rn(fabsf(x[i]), c), __fmul_rn(fabsf(x[i + 1]), c));
-      // sign bit for x < 0 only (-0.0 quantizes to +0.0 in the reference)
-      byte |= (__float_as_uint(x[i]) > 0x80000000u ? 0x08u : 0u) |
-              (__float_as_uint(x[i + 1]) > 0x80000000u ? 0x80u : 0u);
-      nib[i] = byte & 0xfu;
-      nib[i + 1] = byte >> 4;
-      const float2 q = e2m1x2_to_float2(byte);
-      quant[i] = q.x;
-      quant[i + 1] = q.y;
+    for (int w = 0; w < BS / 8; ++w) {
+      float y[8];
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {
+        const float2 t = up2(fma2(pk2(x[8 * w + k], x[8 * w + k + 1]), c2, z2));
+        y[k] = t.x;
+        y[k + 1] = t.y;
+      }
+      codes[w] = e2m1x8_rn(y);
     }
-  } else {
+    write_outputs_hw<BS, FMT>(p, b, codes, s);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
     if (argmin) {
@@ -547,7 +646,6 @@ __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const
       quant[i] = x[i] > 0.0f ? q : (x[i] < 0.0f ? -q : 0.0f);  // torch.sign semantics
       nib[i] = (x[i] < 0.0f ? 8u : 0u) | ((x[i] > 0.0f || x[i] < 0.0f) ? (uint32_t)idx : 0u);
     }
-  }
   }
   const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
   if (p.scales) p.scales[b] = s;
