@@ -710,6 +710,24 @@ __device__ __forceinline__ uint32_t abs_and_amax(const float (&x)[BS], float (&a
   return m;
 }
 
+// Largest magnitude of one block of 16-bit values, as raw 16-bit bits
+// (unsigned compare of sign-cleared bits orders finite values, then inf, then
+// NaN patterns: NaN propagates like torch amax).
+template <int BS>
+__device__ __forceinline__ uint32_t raw_amax16(const unsigned char* raw) {
+  const uint4* p = reinterpret_cast<const uint4*>(raw);
+  uint32_t m2 = 0;
+#pragma unroll
+  for (int v = 0; v < BS / 8; ++v) {
+    const uint4 w = p[v];
+    m2 = __vmaxu2(m2, w.x & 0x7fff7fffu);
+    m2 = __vmaxu2(m2, w.y & 0x7fff7fffu);
+    m2 = __vmaxu2(m2, w.z & 0x7fff7fffu);
+    m2 = __vmaxu2(m2, w.w & 0x7fff7fffu);
+  }
+  return max(m2 & 0xffffu, m2 >> 16);
+}
+
 // Convert one block from raw shared memory to fp32.
 template <int BS, int DT>
 __device__ __forceinline__ void smem_block(const unsigned char* raw, float (&x)[BS]) {
@@ -752,9 +770,15 @@ struct WarpGeom {
   static constexpr int kBytesAligned = (kBytes + 127) / 128 * 128;
 };
 
+// Minimum resident CTAs per SM (register caps), chosen by measurement.
+template <int BS, int FMT, int METHOD>
+struct MinCtas {
+  static constexpr int v = METHOD != kSSE ? 1 : (BS == 16 ? (FMT == kNVFP4 ? 3 : 4) : 2);
+};
+
 // Naive / SSE / argmin methods.
 template <int BS, int FMT, int METHOD, int DT>
-__global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT == kNVFP4 ? 4 : 1) : 2) : 1) quantize_kernel(QuantArgs p) {
+__global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantize_kernel(QuantArgs p) {
   using G = WarpGeom<BS, FMT, DT, METHOD>;
   constexpr int MODE = Mode<FMT, DT>::v;
   constexpr int S = G::kStages;
@@ -805,8 +829,12 @@ __global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT ==
     const int64_t blk = ch * 32 + lane;
     const bool valid = blk < p.n_blocks;
     float x[BS];
-    if (valid) smem_block<BS, DT>(stage + (i % S) * G::kChunkBytes + lane * BS * Elem<DT>::kSize, x);
-    else {
+    uint32_t amax16 = 0;  // 16-bit inputs: amax of the raw magnitudes, two per word
+    if (valid) {
+      const unsigned char* raw = stage + (i % S) * G::kChunkBytes + lane * BS * Elem<DT>::kSize;
+      smem_block<BS, DT>(raw, x);
+      if constexpr (DT != kDtF32) amax16 = raw_amax16<BS>(raw);
+    } else {
 #pragma unroll
       for (int k = 0; k < BS; ++k) x[k] = 0.0f;
     }
@@ -817,7 +845,14 @@ __global__ void __launch_bounds__(kThreads, METHOD == kSSE ? (BS == 16 ? (FMT ==
     }
 
     float a[BS];
-    uint32_t amax_bits = abs_and_amax<BS>(x, a);
+    uint32_t amax_bits;
+    if constexpr (DT == kDtF32) {
+      amax_bits = abs_and_amax<BS>(x, a);
+    } else {
+#pragma unroll
+      for (int k = 0; k < BS; ++k) a[k] = fabsf(x[k]);
+      amax_bits = DT == kDtBF16 ? amax16 << 16 : __float_as_uint(f16_bits_to_float(amax16));
+    }
     float s = naive_scale<FMT>(amax_bits);
     const bool s_nan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
 
@@ -1114,14 +1149,23 @@ template <int BS, int FMT, int METHOD, int DT>
 static cudaError_t launch_q(const QuantArgs& p, int num_sms, cudaStream_t st) {
   using G = WarpGeom<BS, FMT, DT, METHOD>;
   const int smem = kWarps * G::kBytesAligned;
-  cudaError_t e = cudaFuncSetAttribute(quantize_kernel<BS, FMT, METHOD, DT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // Set up once per instantiation and device (a benign race: every thread
+  // computes the same values).
+  static int s_per_sm[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &per_sm, quantize_kernel<BS, FMT, METHOD, DT>, kThreads, smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) per_sm = 1;
+  int per_sm = dev < 64 ? s_per_sm[dev] : 0;
+  if (per_sm == 0) {
+    e = cudaFuncSetAttribute(quantize_kernel<BS, FMT, METHOD, DT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_kernel<BS, FMT, METHOD, DT>, kThreads,
+                                                      smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    if (dev < 64) s_per_sm[dev] = per_sm;
+  }
   const int64_t n_chunks = (p.n_blocks + 31) / 32;
   int64_t want = (n_chunks + kWarps - 1) / kWarps;
   int64_t cap = (int64_t)num_sms * per_sm;
