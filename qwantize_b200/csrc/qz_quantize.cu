@@ -155,11 +155,17 @@ __device__ __forceinline__ float block_sse_hw(const float (&a)[BS], float s, flo
   const uint64_t c2 = pk2(c, c), ms2 = pk2(-s, -s);
 #pragma unroll
   for (int i = 0; i < BS; i += 2) {
-    const uint64_t a2 = pk2(a[i], a[i + 1]);
-    const float2 y = up2(mul2(a2, c2));
-    const float2 q = e2m1x2_to_float2(e2m1x2_rn(y.x, y.y));
-    const uint64_t d = fma2(pk2(q.x, q.y), ms2, a2);
-    sq[i / 2] = mul2(d, d);
+    // y = a*c, q = E2M1(y) decoded through f16, d = a - q*s, d*d: one chain,
+    // the code byte never leaves its 8-bit register
+    uint64_t r;
+    asm("{\n .reg .b64 a2, y, q2, d;\n .reg .f32 y0, y1, q0, q1;\n .reg .b8 b;\n .reg .b32 h;\n"
+        " .reg .b16 lo, hi;\n"
+        " mov.b64 a2, {%1, %2};\n mul.rn.f32x2 y, a2, %3;\n mov.b64 {y0, y1}, y;\n"
+        " cvt.rn.satfinite.e2m1x2.f32 b, y1, y0;\n cvt.rn.f16x2.e2m1x2 h, b;\n mov.b32 {lo, hi}, h;\n"
+        " cvt.f32.f16 q0, lo;\n cvt.f32.f16 q1, hi;\n mov.b64 q2, {q0, q1};\n"
+        " fma.rn.f32x2 d, q2, %4, a2;\n mul.rn.f32x2 %0, d, d;\n}\n"
+        : "=l"(r) : "f"(a[i]), "f"(a[i + 1]), "l"(c2), "l"(ms2));
+    sq[i / 2] = r;
   }
   return sum8_pairs<BS>(sq);
 }
@@ -167,32 +173,22 @@ __device__ __forceinline__ float block_sse_hw(const float (&a)[BS], float s, flo
 // NVFP4 variant: the decoded codes stay in f16 and feed a mixed-precision FMA
 // (f16 x f16 + f32 -> f32): d = RN(a - q*s) with -s held exactly in f16 (every
 // E4M3 value is a normal f16), saving the f16 -> f32 conversions.
-__device__ __forceinline__ float2 fma2_f16(uint32_t q_h2, uint32_t neg_s_h, float a0, float a1) {
-  float d0, d1;
-  asm("{\n .reg .b16 lo, hi, s;\n mov.b32 {lo, hi}, %2;\n cvt.u16.u32 s, %3;\n"
-      " fma.rn.f32.f16 %0, lo, s, %4;\n fma.rn.f32.f16 %1, hi, s, %5;\n}\n"
-      : "=f"(d0), "=f"(d1)
-      : "r"(q_h2), "r"(neg_s_h), "f"(a0), "f"(a1));
-  return make_float2(d0, d1);
-}
-
-__device__ __forceinline__ uint32_t e2m1x2_to_half2_bits(uint32_t byte) {
-  uint32_t h2;
-  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}\n" : "=r"(h2) : "r"(byte));
-  return h2;
-}
-
 template <int BS>
 __device__ __forceinline__ float block_sse_hw_nv(const float (&a)[BS], uint32_t neg_s_h, float c) {
   uint64_t sq[BS / 2];
   const uint64_t c2 = pk2(c, c);
+  const unsigned short ns = (unsigned short)neg_s_h;
 #pragma unroll
   for (int i = 0; i < BS; i += 2) {
-    const float2 y = up2(mul2(pk2(a[i], a[i + 1]), c2));
-    const uint32_t q = e2m1x2_to_half2_bits(e2m1x2_rn(y.x, y.y));
-    const float2 d = fma2_f16(q, neg_s_h, a[i], a[i + 1]);
-    const uint64_t d2 = pk2(d.x, d.y);
-    sq[i / 2] = mul2(d2, d2);
+    uint64_t r;
+    asm("{\n .reg .b64 a2, y, d;\n .reg .f32 y0, y1, d0, d1;\n .reg .b8 b;\n .reg .b32 h;\n"
+        " .reg .b16 lo, hi;\n"
+        " mov.b64 a2, {%1, %2};\n mul.rn.f32x2 y, a2, %3;\n mov.b64 {y0, y1}, y;\n"
+        " cvt.rn.satfinite.e2m1x2.f32 b, y1, y0;\n cvt.rn.f16x2.e2m1x2 h, b;\n mov.b32 {lo, hi}, h;\n"
+        " fma.rn.f32.f16 d0, lo, %4, %1;\n fma.rn.f32.f16 d1, hi, %4, %2;\n"
+        " mov.b64 d, {d0, d1};\n mul.rn.f32x2 %0, d, d;\n}\n"
+        : "=l"(r) : "f"(a[i]), "f"(a[i + 1]), "l"(c2), "h"(ns));
+    sq[i / 2] = r;
   }
   return sum8_pairs<BS>(sq);
 }
