@@ -759,7 +759,7 @@ struct WarpGeom {
   static constexpr int kChunkBytes = 32 * BS * Elem<DT>::kSize;  // 1-4 KB
   static constexpr int kStages = kChunkBytes <= 2048 ? 4 : 2;
   static constexpr bool kCoop = METHOD == kSSE && FMT != kMXFP4;
-  static constexpr int kCpi = 2;  // candidate codes per cooperative work item
+  static constexpr int kCpi = 3;  // candidate codes per cooperative work item
   static constexpr int kRowBytes = kCoop ? 32 * BS * 4 : 0;     // |x| rows for cooperation
   static constexpr int kBytes = kStages * kChunkBytes + kRowBytes + (kCoop ? 32 * 8 + 64 * 4 : 0) +
                                 kStages * 8;
@@ -875,12 +875,20 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
         E0 = base_sse<BS, MODE, DT, FMT>(a, s);
         search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
       }
-      // Work items of CPI consecutive codes of one block: the lookup, the row
-      // reload and the atomic are paid once per item (the last item of a
-      // block repeats its highest code, which cannot change the minimum).
+      // Work items of CPI consecutive candidates of one block: the lookup, the
+      // row reload and the atomic are paid once per item (the last item of a
+      // block repeats its highest candidate, which cannot change the minimum).
+      // The naive scale's own code is dropped when it is an end of [lo, hi]
+      // (its SSE is E0 bit for bit and E0's key wins ties); it usually is lo.
       constexpr int CPI = G::kCpi;
+      if (hi >= lo) {
+        const int cn = FMT == kTable ? table_count_below(s, false) : (int)e4m3_code(s);
+        if (cn == lo) ++lo;
+        else if (cn == hi) --hi;
+      }
       const int n = hi >= lo ? hi - lo + 1 : 0;
       const int n_items = (n + CPI - 1) / CPI;
+
       float4* row = reinterpret_cast<float4*>(rows + lane * BS);
 #pragma unroll
       for (int v = 0; v < BS / 4; ++v) row[v] = make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
