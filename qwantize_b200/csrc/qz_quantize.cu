@@ -197,8 +197,7 @@ __device__ __forceinline__ float block_sse_hw_nv(const float (&a)[BS], uint32_t 
 // E4M3 code (1..126) or UE8M0 biased exponent (1..254).
 struct CandTable {
   float val[256];
-  float c[256];
-  uint32_t neg_h[256];  // f16 bits of -val (NVFP4)
+  uint2 cn[256];         // x: bits of the biased reciprocal c; y: f16 bits of -val (NVFP4)
   float mid[256];       // kTable: midpoints (t[i] + t[i+1]) * 0.5 of snap_to_table
   int n;                // number of candidate codes (kTable: table length)
 };
@@ -214,8 +213,7 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
       const float v = i < n_table ? table[i] : 1.0f;
       t.val[i] = v;
-      t.c[i] = 0.0f;
-      t.neg_h[i] = 0u;
+      t.cn[i] = make_uint2(0u, 0u);
       t.mid[i] = i + 1 < n_table ? __fmul_rn(__fadd_rn(table[i], table[i + 1]), 0.5f) : 0.0f;
     }
     if (threadIdx.x == 0) t.n = n_table;
@@ -226,16 +224,20 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table
     const bool ok = FMT == kNVFP4 ? (i >= 1 && i <= 126) : (i >= 1 && i <= 254);
     const float v = ok ? (FMT == kNVFP4 ? e4m3_value(i) : pow2f(i - 127)) : 1.0f;
     t.val[i] = v;
-    t.c[i] = __fmul_rn(__frcp_rn(v), kBiasDown);
-    t.neg_h[i] = FMT == kNVFP4 ? (uint32_t)__half_as_ushort(__float2half_rn(-v)) : 0u;
+    t.cn[i] = make_uint2(__float_as_uint(__fmul_rn(__frcp_rn(v), kBiasDown)),
+                         FMT == kNVFP4 ? (uint32_t)__half_as_ushort(__float2half_rn(-v)) : 0u);
   }
 }
 
 // Candidate SSE: the hardware path for 16-bit inputs, IEEE division for fp32.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
-  if constexpr (DT != kDtF32 && FMT == kNVFP4) return block_sse_hw_nv<BS>(a, t.neg_h[code], t.c[code]);
-  else if constexpr (DT != kDtF32 && FMT == kMXFP4) return block_sse_hw<BS>(a, t.val[code], t.c[code]);
+  if constexpr (DT != kDtF32 && FMT == kNVFP4) {
+    const uint2 e = t.cn[code];
+    return block_sse_hw_nv<BS>(a, e.y, __uint_as_float(e.x));
+  } else if constexpr (DT != kDtF32 && FMT == kMXFP4) {
+    return block_sse_hw<BS>(a, t.val[code], __uint_as_float(t.cn[code].x));
+  }
   else return block_sse<BS, MODE>(a, t.val[code]);
 }
 
