@@ -213,3 +213,27 @@ def quantize_table(x, bs, method, table, H=None, bf16=True):
     L.qzo_quantize_table(x.ctypes.data, dt, n_blocks, bs, method, t.ctypes.data, t.size, _ptr(H), J,
                          scales.ctypes.data, quants.ctypes.data, dq.ctypes.data)
     return scales, quants, dq
+
+
+FMT_NVINT4, FMT_INT8 = 3, 4
+
+
+def quantize_int(x, bs, fmt, method, H=None, bf16=True):
+    """qzo_quantize_int: NVINT4 (fmt 3, bs 16/32) or INT8 (fmt 4, bs 32..256)."""
+    x = np.ascontiguousarray(x).reshape(-1)
+    n_blocks = x.size // bs
+    dt = _dtype_code(x, bf16)
+    scales = np.empty(n_blocks, np.float32)
+    quants = np.empty(n_blocks * bs, np.float32)
+    dq = np.empty(n_blocks * bs, np.float32)
+    J = 0
+    if method == M_HESSIAN:
+        H = np.ascontiguousarray(H, np.float32)
+        J = H.shape[0]
+    L = lib()
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    L.qzo_quantize_int.argtypes = [vp, i32, i64, i32, i32, i32, vp, i64, vp, vp, vp]
+    L.qzo_quantize_int.restype = i64
+    L.qzo_quantize_int(x.ctypes.data, dt, n_blocks, bs, fmt, method, _ptr(H), J,
+                       scales.ctypes.data, quants.ctypes.data, dq.ctypes.data)
+    return scales, quants, dq

@@ -16,6 +16,11 @@ Outputs (all small; large cases are stored as SHA-256 digests):
   metrics_small.npz    compute_metrics on seeded W / W_dq / X
   unpack_lut.npz       fp4_unpack's decode table read from fp4.py's source
                        (the Triton kernel needs a GPU, so it is read as text)
+  int_small.npz        NVINT4 (bs 16/32) and INT8 (bs 32..256) naive / optimal
+                       on the small weight, the edge blocks and exact INT4
+                       round-half-even ties; H-optimal with X and with H_blocks
+
+``--only int`` regenerates int_small.npz alone.
 """
 from __future__ import annotations
 
@@ -113,7 +118,47 @@ def ref_block_hessians(X: torch.Tensor, bs: int) -> torch.Tensor:
     return H
 
 
-def main(ref_root: str, skip_digests: bool = False):
+def int_tie_blocks() -> torch.Tensor:
+    """(n, 32) rows whose naive NVINT4 scale is 0.25 (amax 1.75) with elements
+    on exact half-integer multiples of it, both signs (round half to even)."""
+    rows = []
+    half = (torch.arange(7) + 0.5) * 0.25
+    for k in range(4):
+        r = torch.cat([half, -half, half.flip(0), -half.flip(0), torch.tensor([1.75, -1.75, 0.0, -0.0])])
+        rows.append(torch.roll(r, 5 * k))
+    r = torch.full((32,), 0.125); r[0] = 1.75; rows.append(r)     # all at 0.5 * s: round to 0
+    r = torch.full((32,), -0.375); r[0] = 1.75; rows.append(r)    # 1.5 * s: round to -2
+    return torch.stack(rows)
+
+
+def make_int(q, W, E, Wh, X):
+    """NVINT4 / INT8 fixtures (nvint4/reference.py, int8/reference.py)."""
+    T_ = int_tie_blocks().to(torch.bfloat16)
+    E256 = E.reshape(-1, 256)
+    out = {"W": bits(W), "E": bits(E), "T": bits(T_), "Wh": bits(Wh)}
+    for name, bss in (("nvint4", (16, 32)), ("int8", (32, 64, 128, 256))):
+        for bs in bss:
+            for src_name, src in (("W", W), ("E", E256 if name == "int8" else E), ("T", T_)):
+                if name == "int8" and src_name == "T":
+                    continue
+                Wb = src.reshape(src.shape[0], -1, bs)
+                for fn in ("naive", "optimal"):
+                    s, qq, dq = getattr(q, f"{name}_{fn}")(Wb, return_dequant=True)
+                    key = f"{name}_{src_name}_{fn}_{bs}"
+                    out[key + "_scales"], out[key + "_quants"], out[key + "_dq"] = s.numpy(), qq.numpy(), dq.numpy()
+            M, K = Wh.shape
+            H = ref_block_hessians(X, bs)
+            out[f"{name}_H_{bs}"] = H.numpy()
+            Wb = Wh.reshape(M, K // bs, bs)
+            fn = getattr(q, f"{name}_optimal_hessian")
+            s, qq, dq = fn(Wb, return_dequant=True, H_blocks=H)
+            out[f"{name}_hH_{bs}_scales"], out[f"{name}_hH_{bs}_quants"] = s.numpy(), qq.numpy()
+            s, qq, dq = fn(Wb, return_dequant=True, X=X)
+            out[f"{name}_hX_{bs}_scales"] = s.numpy()
+    np.savez_compressed(os.path.join(HERE, "int_small.npz"), **out)
+
+
+def main(ref_root: str, skip_digests: bool = False, only: str = None):
     sys.path.insert(0, ref_root)
     import qwantize as q
 
@@ -122,6 +167,11 @@ def main(ref_root: str, skip_digests: bool = False):
     # ---- small quantization fixtures --------------------------------------
     W = make_weight(48, 1024, seed=11)
     E = edge_blocks().to(torch.bfloat16)
+    if only == "int":
+        Wh = make_weight(64, 512, seed=21)
+        X = make_activations(4096, 512, seed=22, chunk_tokens=2048)
+        make_int(q, W, E, Wh, X)
+        return
     out = {"W": bits(W), "E": bits(E)}
     for bs in (16, 32):
         for src_name, src in (("W", W), ("E", E)):
@@ -163,6 +213,7 @@ def main(ref_root: str, skip_digests: bool = False):
         s, qq, dq = q.nvfp4_admm(Wb, return_dequant=True, X=X)
         hout[f"admm_X_{bs}_scales"], hout[f"admm_X_{bs}_quants"] = s.numpy(), qq.numpy()
     np.savez_compressed(os.path.join(HERE, "hessian_small.npz"), **hout)
+    make_int(q, W, E, Wh, X)
 
     # ---- GPTQ (experiments/quant_gptq_strided.py:49-135) on the same W and
     # H = X^T X / T (double, rounded once), with the reference's own quantizers
@@ -243,5 +294,6 @@ def main(ref_root: str, skip_digests: bool = False):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference",
-         skip_digests="--skip-digests" in sys.argv)
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    main(args[0] if args else "/root/reference", skip_digests="--skip-digests" in sys.argv,
+         only="int" if "--only" in sys.argv and "int" in sys.argv else None)
