@@ -50,6 +50,11 @@ extern "C" {
 /* formats */
 #define QZ_FMT_NVFP4 0 /* E2M1 codes, FP8-E4M3 scale per block (126 positive values) */
 #define QZ_FMT_MXFP4 1 /* E2M1 codes, UE8M0 power-of-two scale per block (254 values) */
+/* 2 is the caller-supplied scale table of qz_quantize_table */
+#define QZ_FMT_NVINT4 3 /* int codes in [-7, 7], FP8-E4M3 scale per block; block 16 or 32
+                           (nvint4/reference.py:55-308) */
+#define QZ_FMT_INT8 4   /* int codes in [-127, 127], scale = E4M3 value / 127; block 32, 64,
+                           128 or 256 (int8/reference.py:87-389) */
 
 /* scale-selection methods */
 #define QZ_METHOD_NAIVE 0        /* nvfp4/reference.py:89-126, mxfp4/reference.py:89-129 */
@@ -78,6 +83,13 @@ extern "C" {
  *   packed      (n_blocks*bs/2) E2M1 nibbles; element 2i in the low nibble of
  *               byte i, bit 3 = sign (the layout fp4.py:117-282 decodes)
  *   dq_bf16     (n_blocks*bs) bf16 dequant (exact: dequant values fit bf16)
+ * The integer formats (QZ_FMT_NVINT4, QZ_FMT_INT8; methods NAIVE, SSE and
+ * HESSIAN) write `quants` as the integer values, `scale_codes` as the E4M3
+ * byte of the scale (NVINT4) or of 127 * scale (INT8), `packed` as two's
+ * complement nibbles, element 2i in the low nibble of byte i (NVINT4,
+ * n_blocks*bs/2 bytes) or one int8 per element (INT8, n_blocks*bs bytes), with
+ * 0x8 / 0x80 marking a NaN quant, and `dq_bf16` rounded to nearest (INT8
+ * dequant values need not fit bf16).
  */
 QZ_API int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, int format,
                 int method, const float* h_blocks, int64_t n_col_blocks, float* scales,

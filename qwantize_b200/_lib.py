@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(HERE, "libqwantize_b200.so")
 QZ_OK, QZ_ERR_INVALID, QZ_ERR_CUDA, QZ_ERR_TIMEOUT, QZ_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FMT_NVFP4, FMT_MXFP4 = 0, 1
+FMT_NVINT4, FMT_INT8 = 3, 4  # symmetric integer grids (nvint4/, int8/ of the reference)
 METHOD_NAIVE, METHOD_SSE, METHOD_HESSIAN, METHOD_NAIVE_ARGMIN, METHOD_TWO_ARGMIN = 0, 1, 2, 3, 4
 GRAM_FULL, GRAM_BLOCKDIAG = 0, 1
 

@@ -28,6 +28,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
 UNITS = {
     "qz_quantize.cu": ["-fmad=false"],
     "qz_elementwise.cu": ["-fmad=false"],
+    "qz_int.cu": ["-fmad=false"],
     "qz_abi.cu": [],
     "qz_gemm.cu": [],
 }

@@ -21,10 +21,10 @@ def cuda_device(t: torch.Tensor) -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
-def _blocks(W: torch.Tensor, dim: int):
+def _blocks(W: torch.Tensor, dim: int, valid=(16, 32)):
     dim = dim % W.ndim
     block_size = W.shape[dim]
-    assert block_size in (16, 32)
+    assert block_size in valid, f"block_size={block_size}, expected one of {tuple(valid)}"
     dev = cuda_device(W)
     x = W.movedim(dim, -1)
     batch_shape = x.shape[:-1]
@@ -38,9 +38,9 @@ def _blocks(W: torch.Tensor, dim: int):
     return dim, block_size, batch_shape, x, dev
 
 
-def quantize_fp32(W, dim, return_dequant, fmt, method, H_blocks=None):
+def quantize_fp32(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(16, 32)):
     """Reference-shaped result: fp32 (scales, quants[, dq])."""
-    dim, bs, batch_shape, x, dev = _blocks(W, dim)
+    dim, bs, batch_shape, x, dev = _blocks(W, dim, valid)
     N = x.shape[0]
     scales = torch.empty(N, dtype=torch.float32, device=dev)
     quants = torch.empty(N, bs, dtype=torch.float32, device=dev)
@@ -62,15 +62,17 @@ def quantize_fp32(W, dim, return_dequant, fmt, method, H_blocks=None):
     return res
 
 
-def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None):
-    """Native storage: (scale_codes uint8, packed uint8 (..., bs/2)[, dq bf16]).
+def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(16, 32)):
+    """Native storage: (scale_codes uint8, packed uint8 (..., bs/2 or bs)[, dq bf16]).
 
-    scale_codes are E4M3 bytes (NVFP4) or UE8M0 biased exponents (MXFP4);
-    packed holds two E2M1 nibbles per byte, element 2i in the low nibble."""
-    dim, bs, batch_shape, x, dev = _blocks(W, dim)
+    scale_codes are E4M3 bytes (NVFP4, NVINT4; INT8: of 127 * scale) or UE8M0
+    biased exponents (MXFP4); packed holds two 4-bit codes per byte, element 2i
+    in the low nibble (INT8: one int8 per element)."""
+    dim, bs, batch_shape, x, dev = _blocks(W, dim, valid)
     N = x.shape[0]
     codes = torch.empty(N, dtype=torch.uint8, device=dev)
-    packed = torch.empty(N, bs // 2, dtype=torch.uint8, device=dev)
+    pw = bs if fmt == L.FMT_INT8 else bs // 2
+    packed = torch.empty(N, pw, dtype=torch.uint8, device=dev)
     dq = torch.empty(N, bs, dtype=torch.bfloat16, device=dev) if return_dequant else None
     J = 0
     if method == L.METHOD_HESSIAN:
@@ -80,17 +82,17 @@ def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None):
         L.ptr(x), L.dtype_code(x.dtype), N, bs, fmt, method, L.ptr(H_blocks), J,
         None, None, None, L.ptr(codes), L.ptr(packed), L.ptr(dq), L.stream_ptr(dev))
     L.check(st, "qz_quantize")
-    res = (codes.reshape(*batch_shape), packed.reshape(*batch_shape, bs // 2))
+    res = (codes.reshape(*batch_shape), packed.reshape(*batch_shape, pw))
     if return_dequant:
         res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim),)
     return res
 
 
-def dequantize(scales, quants, dim=-1):
+def dequantize(scales, quants, dim=-1, valid=(16, 32)):
     """quants * scales.unsqueeze(dim) (nvfp4/reference.py:537-549)."""
     dim = dim % quants.ndim
     bs = quants.shape[dim]
-    assert bs in (16, 32)
+    assert bs in valid, f"block_size={bs}, expected one of {tuple(valid)}"
     dev = cuda_device(quants)
     q = quants.movedim(dim, -1).to(dev, torch.float32).contiguous()
     batch_shape = q.shape[:-1]

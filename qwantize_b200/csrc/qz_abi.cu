@@ -74,11 +74,13 @@ int qz_device_ok(void) {
 
 int qz_scale_table(int format, float* out_host, int* n_out) {
   if (!out_host || !n_out) return fail(QZ_ERR_INVALID, "qz_scale_table: NULL output");
-  if (format == QZ_FMT_NVFP4) {
+  if (format == QZ_FMT_NVFP4 || format == QZ_FMT_NVINT4 || format == QZ_FMT_INT8) {
     int n = 0;
     for (int c = 1; c < 0x7f; ++c) {
       int e = c >> 3, m = c & 7;
-      out_host[n++] = e == 0 ? (float)m / 512.0f : ldexpf(1.0f + m / 8.0f, e - 7);
+      const float v = e == 0 ? (float)m / 512.0f : ldexpf(1.0f + m / 8.0f, e - 7);
+      // INT8: the effective scales E4M3 / 127 (int8/reference.py:151-152), IEEE division
+      out_host[n++] = format == QZ_FMT_INT8 ? v / 127.0f : v;
     }
     *n_out = n;
     return QZ_OK;
@@ -91,10 +93,46 @@ int qz_scale_table(int format, float* out_host, int* n_out) {
   return fail(QZ_ERR_INVALID, "qz_scale_table: unknown format %d", format);
 }
 
+// NVINT4 / INT8 (qz_int.cu): validation and launch.
+static int quantize_int(const void* x, int x_dtype, int64_t n_blocks, int block_size, int format, int method,
+                        const float* h_blocks, int64_t n_col_blocks, float* scales, float* quants, float* dq,
+                        uint8_t* scale_codes, uint8_t* packed, uint16_t* dq_bf16, void* stream) {
+  if (format == QZ_FMT_NVINT4 && block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size=%d, expected one of (16, 32)", block_size);
+  if (format == QZ_FMT_INT8 && block_size != 32 && block_size != 64 && block_size != 128 && block_size != 256)
+    return fail(QZ_ERR_INVALID, "block_size=%d, expected one of (32, 64, 128, 256)", block_size);
+  if (method != QZ_METHOD_NAIVE && method != QZ_METHOD_SSE && method != QZ_METHOD_HESSIAN)
+    return fail(QZ_ERR_INVALID, "the integer formats support the naive, SSE and Hessian methods, got %d", method);
+  if (x_dtype != QZ_DTYPE_F32 && x_dtype != QZ_DTYPE_BF16 && x_dtype != QZ_DTYPE_F16)
+    return fail(QZ_ERR_INVALID, "unknown dtype %d", x_dtype);
+  if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
+  if (n_blocks == 0) return QZ_OK;
+  if (!x || !aligned(x, 16)) return fail(QZ_ERR_INVALID, "x must be non-NULL and 16-byte aligned");
+  if ((quants && !aligned(quants, 4)) || (dq && !aligned(dq, 4)) || (dq_bf16 && !aligned(dq_bf16, 2)))
+    return fail(QZ_ERR_INVALID, "quants/dq must be 4-byte aligned, dq_bf16 2-byte aligned");
+  if (method == QZ_METHOD_HESSIAN) {
+    if (!h_blocks) return fail(QZ_ERR_INVALID, "X or H_blocks required");
+    if (n_col_blocks <= 0 || n_blocks % n_col_blocks != 0 || n_col_blocks > 2147483647LL)
+      return fail(QZ_ERR_INVALID, "n_blocks (%lld) must be a multiple of n_col_blocks (%lld)",
+                  (long long)n_blocks, (long long)n_col_blocks);
+    if (!aligned(h_blocks, 16)) return fail(QZ_ERR_INVALID, "h_blocks must be 16-byte aligned");
+  }
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  QuantArgs p{x, n_blocks, h_blocks, n_col_blocks, scales, quants, dq, scale_codes, packed, dq_bf16};
+  return cuda_status(launch_quantize_int(p, x_dtype, block_size, format, method, sms,
+                                         static_cast<cudaStream_t>(stream)),
+                     "qz_quantize launch (integer format)");
+}
+
 int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, int format,
                 int method, const float* h_blocks, int64_t n_col_blocks, float* scales,
                 float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,
                 uint16_t* dq_bf16, void* stream) {
+  if (format == QZ_FMT_NVINT4 || format == QZ_FMT_INT8)
+    return quantize_int(x, x_dtype, n_blocks, block_size, format, method, h_blocks, n_col_blocks, scales, quants,
+                        dq, scale_codes, packed, dq_bf16, stream);
   if (block_size != 16 && block_size != 32)
     return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
   if (format != QZ_FMT_NVFP4 && format != QZ_FMT_MXFP4)
@@ -188,8 +226,8 @@ int qz_quantize_table(const void* x, int x_dtype, int64_t n_blocks, int block_si
 
 int qz_dequantize(const float* scales, const float* quants, int64_t n_blocks, int block_size,
                   float* out, void* stream) {
-  if (block_size != 16 && block_size != 32)
-    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128 && block_size != 256)
+    return fail(QZ_ERR_INVALID, "block_size must be 16, 32, 64, 128 or 256, got %d", block_size);
   if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
   if (n_blocks == 0) return QZ_OK;
   if (!scales || !quants || !out) return fail(QZ_ERR_INVALID, "NULL pointer");

@@ -18,6 +18,7 @@ namespace qz {
 
 constexpr int kDtF32 = 0, kDtBF16 = 1, kDtF16 = 2;
 constexpr int kNVFP4 = 0, kMXFP4 = 1, kTable = 2;  // kTable: caller-supplied sorted scale table
+constexpr int kNVINT4 = 3, kInt8 = 4;              // symmetric integer grids (qz_int.cu)
 constexpr int kNaive = 0, kSSE = 1, kHessian = 2, kNaiveArgmin = 3, kTwoArgmin = 4;
 
 // NaN bit patterns the reference produces for a NaN scale: the E4M3 NaN code

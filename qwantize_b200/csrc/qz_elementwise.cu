@@ -7,14 +7,16 @@
 
 namespace qz {
 
-// quants * scales with x86 NaN payload propagation (first NaN operand, quieted),
-// which is what the reference's CPU `quants * scales.unsqueeze(dim)` returns.
+// quants * scales with the NaN payload the reference's CPU
+// `quants * scales.unsqueeze(dim)` returns: the scale's NaN if the scale is NaN,
+// else the quant's (quieted); torch's multiply kernel puts its second operand
+// first (measured for broadcast and contiguous operands).
 __device__ __forceinline__ float mul_x86(float q, float s) {
   float r = __fmul_rn(q, s);
   if (r != r) {
     uint32_t qb = __float_as_uint(q), sb = __float_as_uint(s);
-    if (is_nan_bits(qb & 0x7fffffffu)) return __uint_as_float(qb | 0x00400000u);
     if (is_nan_bits(sb & 0x7fffffffu)) return __uint_as_float(sb | 0x00400000u);
+    if (is_nan_bits(qb & 0x7fffffffu)) return __uint_as_float(qb | 0x00400000u);
     return __uint_as_float(0xffc00000u);  // inf * 0: x86 default NaN
   }
   return r;
@@ -139,7 +141,7 @@ cudaError_t launch_dequantize(const float* scales, const float* quants, int64_t 
   int64_t n_vec = n_blocks * bs / 4;
   if (n_vec == 0) return cudaSuccess;
   dequantize_kernel<<<grid_for(n_vec, 256, num_sms), 256, 0, st>>>(
-      scales, reinterpret_cast<const float4*>(quants), n_vec, bs == 16 ? 2 : 3,
+      scales, reinterpret_cast<const float4*>(quants), n_vec, __builtin_ctz((unsigned)bs) - 2,
       reinterpret_cast<float4*>(out));
   return cudaGetLastError();
 }

@@ -352,6 +352,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (trow < p.T) { part0 += (double)e; part1 += (double)r2; }
+      } else if (MODE == kGramDiag && p.bs > 32) {
+        // bs 64 / 128: the rows of this warp belong to one block, whose bs
+        // columns start at cb inside the 128-wide tile (loads are warp-wide)
+        const int bs = p.bs;
+        const int cb = (quarter * 32 / bs) * bs;
+        const int64_t i = mi * kBM + row;
+        float* dst = (nj == 0 ? p.H : p.partials + (nj - 1) * p.K * bs) + (i / bs) * bs * bs + (i % bs) * bs;
+        const bool add = nj == 0 && p.accumulate;
+#pragma unroll 1
+        for (int c = 0; c < bs; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + cb + c, v);
+          if (i < p.K) {
+#pragma unroll
+            for (int q = 0; q < 16; q += 4) {
+              float4 w = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+              float4* d4 = reinterpret_cast<float4*>(dst + c + q);
+              if (add) {
+                const float4 o = *d4;
+                w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+              }
+              *d4 = w;
+            }
+          }
+        }
       } else if (MODE == kGramDiag) {
         // this warp's rows 32q..32q+31 meet the diagonal in columns 32q..32q+31
         float v[32];
@@ -591,8 +616,9 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   if (mode != QZ_GRAM_FULL && mode != QZ_GRAM_BLOCKDIAG) return fail(QZ_ERR_INVALID, "unknown gram mode %d", mode);
   if (T < 0 || K <= 0) return fail(QZ_ERR_INVALID, "need T >= 0 and K > 0");
   if (K % 8 != 0) return fail(QZ_ERR_INVALID, "K must be a multiple of 8 (16-byte rows for TMA)");
-  if (mode == QZ_GRAM_BLOCKDIAG && ((block_size != 16 && block_size != 32) || K % block_size != 0))
-    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32 and divide K");
+  if (mode == QZ_GRAM_BLOCKDIAG &&
+      ((block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128) || K % block_size != 0))
+    return fail(QZ_ERR_INVALID, "block_size must be 16, 32, 64 or 128 and divide K");
   if (K > 2147483647LL || T > 2147483647LL) return fail(QZ_ERR_INVALID, "T and K must fit in int32");
   if (!H) return fail(QZ_ERR_INVALID, "H is NULL");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

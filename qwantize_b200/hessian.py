@@ -19,6 +19,19 @@ def gram(X: torch.Tensor, mode: str = "full", block_size: int = 16, out: torch.T
     Xd = X.to(dev, torch.bfloat16).contiguous()
     T, K = Xd.shape
     m = L.GRAM_FULL if mode == "full" else L.GRAM_BLOCKDIAG
+    if m == L.GRAM_BLOCKDIAG and block_size > 128:
+        # blocks wider than one 128-column diagonal tile: the full Gram of each
+        # contiguous column slice
+        assert K % block_size == 0
+        J = K // block_size
+        if out is None:
+            out = torch.empty((J, block_size, block_size), dtype=torch.float32, device=dev)
+            accumulate = False
+        for j in range(J):
+            xs = Xd[:, j * block_size:(j + 1) * block_size].contiguous()
+            L.check(L.load().qz_gram(L.ptr(xs), T, block_size, L.GRAM_FULL, block_size, int(accumulate),
+                                     L.ptr(out[j]), L.stream_ptr(dev)), "qz_gram")
+        return out
     if m == L.GRAM_BLOCKDIAG:
         assert K % block_size == 0
         shape = (K // block_size, block_size, block_size)
@@ -37,12 +50,12 @@ def block_hessians(X: torch.Tensor, block_size: int) -> torch.Tensor:
     return gram(X, "blockdiag", block_size)
 
 
-def resolve_h_blocks(W: torch.Tensor, dim: int, X, H_blocks) -> torch.Tensor:
+def resolve_h_blocks(W: torch.Tensor, dim: int, X, H_blocks, valid=(16, 32)) -> torch.Tensor:
     """The (J, bs, bs) fp32 device tensor the search uses: H_blocks if given
     (X is then ignored, as in the reference), else built from X."""
     assert X is not None or H_blocks is not None, "X or H_blocks required"
     bs = W.shape[dim % W.ndim]
-    assert bs in (16, 32)
+    assert bs in valid, f"block_size={bs}, expected one of {tuple(valid)}"
     dev = cuda_device(W)
     if H_blocks is not None:
         return H_blocks.to(dev, torch.float32).contiguous()
