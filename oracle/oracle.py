@@ -218,8 +218,9 @@ def quantize_table(x, bs, method, table, H=None, bf16=True):
 FMT_NVINT4, FMT_INT8 = 3, 4
 
 
-def quantize_int(x, bs, fmt, method, H=None, bf16=True):
-    """qzo_quantize_int: NVINT4 (fmt 3, bs 16/32) or INT8 (fmt 4, bs 32..256)."""
+def quantize_int(x, bs, fmt, method, H=None, bf16=True, threads=None):
+    """qzo_quantize_int: NVINT4 (fmt 3, bs 16/32) or INT8 (fmt 4, bs 32..256),
+    block ranges on a thread pool (ctypes releases the GIL)."""
     x = np.ascontiguousarray(x).reshape(-1)
     n_blocks = x.size // bs
     dt = _dtype_code(x, bf16)
@@ -234,6 +235,24 @@ def quantize_int(x, bs, fmt, method, H=None, bf16=True):
     vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
     L.qzo_quantize_int.argtypes = [vp, i32, i64, i32, i32, i32, vp, i64, vp, vp, vp]
     L.qzo_quantize_int.restype = i64
-    L.qzo_quantize_int(x.ctypes.data, dt, n_blocks, bs, fmt, method, _ptr(H), J,
-                       scales.ctypes.data, quants.ctypes.data, dq.ctypes.data)
+    threads = threads or os.cpu_count() or 1
+    esz = x.itemsize
+    if method == M_HESSIAN:
+        step = max(J, ((n_blocks // (threads * 8)) // J) * J or J)
+    else:
+        step = max(256, n_blocks // (threads * 8) + 1)
+    ranges = [(b, min(n_blocks, b + step)) for b in range(0, n_blocks, step)]
+
+    def run(r):
+        b0, b1 = r
+        return L.qzo_quantize_int(x.ctypes.data + b0 * bs * esz, dt, b1 - b0, bs, fmt, method, _ptr(H), J,
+                                  scales.ctypes.data + b0 * 4, quants.ctypes.data + b0 * bs * 4,
+                                  dq.ctypes.data + b0 * bs * 4)
+
+    if len(ranges) == 1 or threads == 1:
+        for r in ranges:
+            run(r)
+    else:
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(run, ranges))
     return scales, quants, dq

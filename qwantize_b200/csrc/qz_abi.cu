@@ -61,6 +61,9 @@ int qz_poll_device_error(int clear, unsigned* flags_out) {
   int st = cuda_status(read_device_error_quantize(&f, clear != 0), "qz_poll_device_error");
   if (st == QZ_OK) st = cuda_status(read_device_error_gemm(&g, clear != 0), "qz_poll_device_error");
   f |= g;
+  g = 0;
+  if (st == QZ_OK) st = cuda_status(read_device_error_int(&g, clear != 0), "qz_poll_device_error");
+  f |= g;
   if (flags_out) *flags_out = f;
   if (st != QZ_OK) return st;
   if (f) return fail(QZ_ERR_TIMEOUT, "a device-side wait gave up (flags 0x%x)", f);

@@ -32,6 +32,7 @@
 
 #include "qz_common.cuh"
 #include "qz_kernels.h"
+#include "qz_ptx.cuh"
 
 namespace qz {
 namespace {
@@ -186,10 +187,17 @@ __device__ __forceinline__ float raw_elem(const unsigned char* raw, int i) {
   return DT == kDtBF16 ? bf16_bits_to_float(h) : f16_bits_to_float(h);
 }
 
+// Per-warp shared memory: a ring of kStages bulk-copy stages of kTiles tiles
+// (four blocks each, raw input), then the sort and residual areas of the four
+// groups, then the stages' mbarriers.
 template <int BS, int DT>
 struct IGeom {
-  static constexpr int kRaw = 4 * BS * Elem<DT>::kSize;  // four blocks, raw
-  static constexpr int kBytes = kRaw + 2 * 4 * BS * 4;    // + sort and residual areas
+  static constexpr int kTile = 4 * BS * Elem<DT>::kSize;
+  static constexpr int kTiles = kTile >= 2048 ? 1 : 2048 / kTile;
+  static constexpr int kStage = kTiles * kTile;
+  static constexpr int kStages = kStage <= 2048 ? 4 : 2;
+  static constexpr int kRing = kStages * kStage;
+  static constexpr int kBytes = kRing + 2 * 4 * BS * 4 + kStages * 8;
 };
 
 template <int BS, int FMT, int METHOD, int DT>
@@ -206,21 +214,49 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = lane >> 3, g = lane & 7;
-  unsigned char* wraw = ismem + warp * G::kBytes;
-  uint32_t* wsort = reinterpret_cast<uint32_t*>(wraw + G::kRaw) + grp * BS;
-  float* wr = reinterpret_cast<float*>(wraw + G::kRaw) + 4 * BS + grp * BS;
+  unsigned char* wbase = ismem + warp * G::kBytes;
+  uint32_t* wsort = reinterpret_cast<uint32_t*>(wbase + G::kRing) + grp * BS;
+  float* wr = reinterpret_cast<float*>(wbase + G::kRing) + 4 * BS + grp * BS;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(wbase + G::kRing + 2 * 4 * BS * 4);
 
-  const int64_t n_tiles = (p.n_blocks + 3) / 4;
-  for (int64_t t = (int64_t)blockIdx.x * kIWarps + warp; t < n_tiles; t += (int64_t)gridDim.x * kIWarps) {
-    const int64_t b0 = t * 4;
+  const int64_t blocks_per_chunk = (int64_t)G::kTiles * 4;
+  const int64_t n_chunks = (p.n_blocks + blocks_per_chunk - 1) / blocks_per_chunk;
+  const int64_t gwarp = (int64_t)blockIdx.x * kIWarps + warp, nwarps = (int64_t)gridDim.x * kIWarps;
+  const char* src = static_cast<const char*>(p.x);
+  auto issue = [&](int64_t i) {  // lane 0: chunk i of this warp into stage i % kStages
+    const int64_t ch = gwarp + i * nwarps;
+    if (ch >= n_chunks) return;
+    const int64_t nb = p.n_blocks - ch * blocks_per_chunk < blocks_per_chunk ? p.n_blocks - ch * blocks_per_chunk
+                                                                          : blocks_per_chunk;
+    const uint32_t bytes = (uint32_t)(nb * BS * Elem<DT>::kSize);
+    uint64_t* bb = bar + (i % G::kStages);
+    mbar_arrive_expect_tx(bb, bytes);
+    bulk_load(wbase + (i % G::kStages) * G::kStage, src + ch * blocks_per_chunk * BS * Elem<DT>::kSize, bytes, bb);
+  };
+  if (lane == 0) {
+    for (int k = 0; k < G::kStages; ++k) mbar_init(bar + k, 1);
+    fence_barrier_init();
+    for (int k = 0; k < G::kStages; ++k) issue(k);
+  }
+  __syncwarp();
+
+  for (int64_t ci = 0;; ++ci) {
+   const int64_t ch = gwarp + ci * nwarps;
+   if (ch >= n_chunks) break;
+   const bool landed = mbar_wait_bounded(bar + (ci % G::kStages), (uint32_t)((ci / G::kStages) & 1),
+                                         kDevErrLoadTimeout);
+   if (!__all_sync(0xffffffffu, landed)) {  // the whole warp leaves together
+     // a copy never landed: drain what this warp still has in flight (bounded), then stop
+     for (int64_t k = ci + 1; k < ci + G::kStages && gwarp + k * nwarps < n_chunks; ++k)
+       mbar_wait_bounded(bar + (k % G::kStages), (uint32_t)((k / G::kStages) & 1), kDevErrLoadTimeout);
+     return;
+   }
+   const unsigned char* stage = wbase + (ci % G::kStages) * G::kStage;
+   for (int tt = 0; tt < G::kTiles; ++tt) {
+    const int64_t b0 = (ch * G::kTiles + tt) * 4;
+    if (b0 >= p.n_blocks) break;
     const int nb = (int)(p.n_blocks - b0 < 4 ? p.n_blocks - b0 : 4);
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(p.x) +
-                                                        b0 * BS * Elem<DT>::kSize);
-      const int n16 = nb * BS * Elem<DT>::kSize / 16;
-      for (int i = lane; i < n16; i += 32) reinterpret_cast<uint4*>(wraw)[i] = __ldg(src + i);
-    }
-    __syncwarp();
+    const unsigned char* wraw = stage + tt * G::kTile;
     const bool valid = grp < nb;
     const int64_t b = b0 + grp;
     float x[NE];
@@ -359,7 +395,12 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
       if (p.scales) p.scales[b] = s;
       if (p.scale_codes) p.scale_codes[b] = (uint8_t)code;
     }
-    __syncwarp();  // wraw is reloaded for the next tile
+   }
+   __syncwarp();  // the stage is refilled below
+   if (lane == 0) {
+     fence_proxy_async_smem();
+     issue(ci + G::kStages);
+   }
   }
 }
 
@@ -380,8 +421,8 @@ cudaError_t launch_int_k(const QuantArgs& p, int num_sms, cudaStream_t st) {
     if (per_sm < 1) per_sm = 1;
     if (dev < 64) s_per_sm[dev] = per_sm;
   }
-  const int64_t n_tiles = (p.n_blocks + 3) / 4;
-  const int64_t want = (n_tiles + kIWarps - 1) / kIWarps;
+  const int64_t n_chunks = (p.n_blocks + G::kTiles * 4 - 1) / (G::kTiles * 4);
+  const int64_t want = (n_chunks + kIWarps - 1) / kIWarps;
   const int64_t cap = (int64_t)num_sms * per_sm;
   const unsigned grid = (unsigned)(want < cap ? want : cap);
   int_kernel<BS, FMT, METHOD, DT><<<grid, kIThreads, smem, st>>>(p);
@@ -408,6 +449,13 @@ cudaError_t launch_int_d(const QuantArgs& p, int dtype, int method, int num_sms,
 }
 
 }  // namespace
+
+cudaError_t read_device_error_int(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, qz_device_error, sizeof(unsigned));
+  if (e != cudaSuccess || !clear) return e;
+  unsigned zero = 0;
+  return cudaMemcpyToSymbol(qz_device_error, &zero, sizeof(unsigned));
+}
 
 cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, int method, int num_sms,
                                 cudaStream_t st) {

@@ -40,5 +40,6 @@ cudaError_t launch_weight_sums(const void* W, int wdt, const void* Wdq, int ddt,
 
 cudaError_t read_device_error_quantize(unsigned* out, bool clear);
 cudaError_t read_device_error_gemm(unsigned* out, bool clear);
+cudaError_t read_device_error_int(unsigned* out, bool clear);
 
 }  // namespace qz

@@ -20,7 +20,9 @@ Outputs (all small; large cases are stored as SHA-256 digests):
                        on the small weight, the edge blocks and exact INT4
                        round-half-even ties; H-optimal with X and with H_blocks
 
-``--only int`` regenerates int_small.npz alone.
+``--only int`` regenerates int_small.npz alone; ``--only int-digests`` writes
+int_digests.json (SHA-256 of the NVINT4 / INT8 outputs on the full config-0/1
+weight).
 """
 from __future__ import annotations
 
@@ -158,6 +160,23 @@ def make_int(q, W, E, Wh, X):
     np.savez_compressed(os.path.join(HERE, "int_small.npz"), **out)
 
 
+def make_int_digests(q):
+    """SHA-256 of the reference's NVINT4 / INT8 naive and optimal outputs on the
+    full 2560x9728 config-0/1 weight (seed 0): int_digests.json."""
+    Wf = make_weight(2560, 9728, seed=0)
+    dg = {"weight_sha256": hashlib.sha256(bits(Wf).tobytes()).hexdigest(),
+          "M": 2560, "K": 9728, "seed": 0, "torch": torch.__version__}
+    for name, bss in (("nvint4", (16, 32)), ("int8", (32, 64, 128, 256))):
+        for bs in bss:
+            Wb = Wf.reshape(2560, 9728 // bs, bs)
+            for fn in ("naive", "optimal"):
+                s, qq, dq = getattr(q, f"{name}_{fn}")(Wb, return_dequant=True)
+                dg[f"{name}_{fn}_{bs}"] = {"scales": digest(s), "quants": digest(qq), "dq": digest(dq)}
+                print(name, fn, bs, flush=True)
+    with open(os.path.join(HERE, "int_digests.json"), "w") as f:
+        json.dump(dg, f, indent=1, sort_keys=True)
+
+
 def main(ref_root: str, skip_digests: bool = False, only: str = None):
     sys.path.insert(0, ref_root)
     import qwantize as q
@@ -167,6 +186,9 @@ def main(ref_root: str, skip_digests: bool = False, only: str = None):
     # ---- small quantization fixtures --------------------------------------
     W = make_weight(48, 1024, seed=11)
     E = edge_blocks().to(torch.bfloat16)
+    if only == "int-digests":
+        make_int_digests(q)
+        return
     if only == "int":
         Wh = make_weight(64, 512, seed=21)
         X = make_activations(4096, 512, seed=22, chunk_tokens=2048)
@@ -294,6 +316,7 @@ def main(ref_root: str, skip_digests: bool = False, only: str = None):
 
 
 if __name__ == "__main__":
-    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    args = [a for i, a in enumerate(sys.argv[1:], 1)
+            if not a.startswith("--") and sys.argv[i - 1] != "--only"]
     main(args[0] if args else "/root/reference", skip_digests="--skip-digests" in sys.argv,
-         only="int" if "--only" in sys.argv and "int" in sys.argv else None)
+         only=sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None)

@@ -147,3 +147,23 @@ def test_int_dequantize_and_errors():
         q.int8_naive(_bf(g["W"]).to(DEV).reshape(48, -1, 16))
     with pytest.raises(AssertionError):
         q.int8_optimal_hessian(W8)
+
+
+@pytest.mark.parametrize("name,fmt,bs", INT_CASES)
+def test_int_full_config_digests(name, fmt, bs):
+    """Full 2560x9728 config-0/1 weight: SHA-256 of every output equals the
+    digest of the reference's own output (int_digests.json)."""
+    import hashlib
+    import json
+    import os
+    from qwantize_b200.synthetic import make_weight
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "int_digests.json")) as f:
+        d = json.load(f)
+    W = make_weight(d["M"], d["K"], d["seed"])
+    assert hashlib.sha256(W.view(torch.int16).numpy().tobytes()).hexdigest() == d["weight_sha256"]
+    Wb = W.to(DEV).reshape(d["M"], d["K"] // bs, bs)
+    for method in ("naive", "optimal"):
+        s, qq, dq = getattr(_mod(name), f"{name}_{method}")(Wb, return_dequant=True)
+        ref = d[f"{name}_{method}_{bs}"]
+        for t, k in ((s, "scales"), (qq, "quants"), (dq, "dq")):
+            assert hashlib.sha256(t.cpu().numpy().tobytes()).hexdigest() == ref[k], (method, k)

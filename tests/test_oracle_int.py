@@ -48,3 +48,25 @@ def test_int_ties_round_half_even(oracle):
     half = np.abs(xf / 0.25 - np.round(xf / 0.25)) == 0.5
     assert half.sum() > 50
     assert (np.abs(q[half]) % 2 == 0).all()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name,fmt,bs", INT_CASES)
+def test_oracle_int_full_config_digests(oracle, name, fmt, bs):
+    """Full 2560x9728 weight: the oracle's outputs hash to the reference's."""
+    import hashlib
+    import json
+    import os
+
+    import torch
+
+    from qwantize_b200.synthetic import make_weight
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "int_digests.json")) as f:
+        d = json.load(f)
+    W = make_weight(d["M"], d["K"], d["seed"])
+    wb = W.view(torch.int16).numpy().view(np.uint16)
+    for mi, method in ((0, "naive"), (1, "optimal")):
+        s, q, dq = oracle.quantize_int(wb, bs, fmt, mi)
+        ref = d[f"{name}_{method}_{bs}"]
+        for t, k in ((s, "scales"), (q, "quants"), (dq, "dq")):
+            assert hashlib.sha256(t.tobytes()).hexdigest() == ref[k], (method, k)
