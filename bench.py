@@ -32,6 +32,7 @@ sys.path.insert(0, ROOT)
 
 M, K = 2560, 9728
 WEIGHTS = M * K
+INST_PER_WEIGHT_NVFP4_SSE_BS16 = 138.9  # ncu: 108,057,803 warp instructions x 32 / 24,903,680 weights
 CALLS = [(fmt, bs, meth) for fmt in (0, 1) for bs in (16, 32) for meth in (0, 1)]  # 8 per step
 FMT_NAME = {0: "nvfp4", 1: "mxfp4"}
 METH_NAME = {0: "naive", 1: "optimal"}
@@ -316,18 +317,19 @@ def bench_ours(args):
 
     if rank == 0:
         issue = None
-        if meth == 1 and nc is not None:
-            # lane-op cost model fixed before building: 12 per element for the
-            # bounds, 10 per element per full SSE evaluation (baseline + each
-            # candidate), 4 per element per clip check
-            ops_per_w = 12 + 10 * (1 + nc) + 4 * nc
+        if meth == 1:
+            # Instruction-issue roofline of the dominant kernel: thread
+            # instructions per weight from ncu (smsp__inst_executed.sum x 32 /
+            # weights of one launch, profiles/quantize_nvfp4_sse_bs16_config1.md)
+            # over the issue peak of 148 SMs x 4 schedulers x 32 lanes per clock.
+            inst_per_w = INST_PER_WEIGHT_NVFP4_SSE_BS16
             clk = clk.summary()
             mhz = clk.get("sm_mhz") or 1965.0
             peak_ops = 148 * 128 * mhz * 1e6
-            ach_ops = WEIGHTS * ops_per_w / (per[dom] / 1e3)
-            issue = {"unit": "lane-op/s", "achieved": ach_ops, "peak": peak_ops, "frac": ach_ops / peak_ops,
-                     "candidates_per_block": nc, "lane_ops_per_weight": ops_per_w,
-                     "peak_basis": "148 SMs x 128 FP32 lanes x median SM clock"}
+            ach_ops = WEIGHTS * inst_per_w / (per[dom] / 1e3)
+            issue = {"unit": "thread-instr/s", "achieved": ach_ops, "peak": peak_ops, "frac": ach_ops / peak_ops,
+                     "instr_per_weight": inst_per_w, "candidates_per_block": nc,
+                     "peak_basis": "148 SMs x 4 schedulers x 32 lanes x median SM clock"}
         else:
             clk = clk.summary()
         line = {
@@ -430,6 +432,25 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         "nvfp4_admm_bs16_ms": ms_admm,
         "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
         "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9}
+    # NVINT4 / INT8 on the config-1 weight (native outputs: scale bytes, packed codes, bf16 dequant)
+    Lq = _lib.load()
+    n_w = 2560 * Kx
+    ints = {}
+    c_buf = torch.empty(n_w // 16, dtype=torch.uint8, device=device)
+    p_buf = torch.empty(n_w, dtype=torch.uint8, device=device)
+    d_buf = torch.empty(n_w, dtype=torch.bfloat16, device=device)
+    for fmt, tag, bss in ((_lib.FMT_NVINT4, "nvint4", (16, 32)), (_lib.FMT_INT8, "int8", (32, 64, 128, 256))):
+        for bs in bss:
+            for meth, mname in ((0, "naive"), (1, "optimal")):
+                def run_int(fmt=fmt, bs=bs, meth=meth):
+                    Lq.qz_quantize(W.data_ptr(), 1, n_w // bs, bs, fmt, meth, None, 0, None, None, None,
+                                   c_buf.data_ptr(), p_buf.data_ptr(), d_buf.data_ptr(), stream.cuda_stream)
+                ms_i = _ev_time(run_int, stream, 5)
+                ints[f"{tag}_{mname}_bs{bs}_ms"] = ms_i
+                ints[f"{tag}_{mname}_bs{bs}_gweights_per_s"] = n_w / (ms_i / 1e3) / 1e9
+    ints["nvint4_hoptimal_bs16_search_ms"] = _ev_time(lambda: q.nvint4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    out["config1_int_formats"] = ints
+    del c_buf, p_buf, d_buf
     # GPTQ (NVFP4 bs16 SSE-optimal) of the 2560x9728 weight on the full H / T
     from qwantize_b200.gptq import gptq
     H.div_(T)
