@@ -130,6 +130,50 @@ __device__ __forceinline__ float int_sse(const float (&x)[BS / 8], float s, floa
   return group_sum<BS>(d2);
 }
 
+// One element's squared error for |x| = a at a candidate scale s > 0 (finite).
+template <int FMT, int DT>
+__device__ __forceinline__ float int_d2(float a, float s, float rc) {
+  float d;
+  if constexpr (FMT == kNVINT4 && DT != kDtF32) {
+    const float q = fminf(rintf(__fmul_rn(a, rc)), 7.0f);
+    d = __fmaf_rn(-q, s, a);
+  } else {
+    float q = rintf(__fdiv_rn(a, s));
+    q = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
+    d = __fsub_rn(a, __fmul_rn(q, s));
+  }
+  return __fmul_rn(d, d);
+}
+
+// A whole block's SSE evaluated by one lane, in torch's row-sum order (rows of
+// 16: acc[k] = v[k] + v[k+8]; longer rows: per residue m, four stride-32
+// accumulators combined in order), folded residue by residue.
+template <int BS, int FMT, int DT, class ROW>
+__device__ __forceinline__ float lane_row_sse(const ROW& ax, float s, float rc) {
+  float r = 0.0f;
+  if constexpr (BS == 16) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float a = __fadd_rn(int_d2<FMT, DT>(ax[k], s, rc), int_d2<FMT, DT>(ax[k + 8], s, rc));
+      r = k ? __fadd_rn(r, a) : a;
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      float A[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        A[t] = int_d2<FMT, DT>(ax[m + 8 * t], s, rc);
+#pragma unroll
+        for (int jj = 1; jj < BS / 32; ++jj) A[t] = __fadd_rn(A[t], int_d2<FMT, DT>(ax[m + 8 * t + 32 * jj], s, rc));
+      }
+      const float a = __fadd_rn(__fadd_rn(__fadd_rn(A[0], A[1]), A[2]), A[3]);
+      r = m ? __fadd_rn(r, a) : a;
+    }
+  }
+  return r;
+}
+
 // sum(clamp(|x| - Q s, 0)^2) (nvint4/reference.py:144, int8/reference.py:200).
 template <int BS, int FMT>
 __device__ __forceinline__ float int_clip(const float (&x)[BS / 8], float s) {
@@ -188,8 +232,9 @@ __device__ __forceinline__ float raw_elem(const unsigned char* raw, int i) {
 }
 
 // Per-warp shared memory: a ring of kStages bulk-copy stages of kTiles tiles
-// (four blocks each, raw input), then the sort and residual areas of the four
-// groups, then the stages' mbarriers.
+// (four blocks each, raw input), then two areas of one padded row per group
+// (sort keys; |x| for the SSE search or the residual of the Hessian), then the
+// stages' mbarriers.
 template <int BS, int DT>
 struct IGeom {
   static constexpr int kTile = 4 * BS * Elem<DT>::kSize;
@@ -197,7 +242,9 @@ struct IGeom {
   static constexpr int kStage = kTiles * kTile;
   static constexpr int kStages = kStage <= 2048 ? 4 : 2;
   static constexpr int kRing = kStages * kStage;
-  static constexpr int kBytes = kRing + 2 * 4 * BS * 4 + kStages * 8;
+  static constexpr int kRow = BS + 4;  // padded per-group row (floats): no bank conflicts across groups
+  static constexpr int kArea = 4 * kRow * 4;
+  static constexpr int kBytes = kRing + 2 * kArea + kStages * 8;
 };
 
 template <int BS, int FMT, int METHOD, int DT>
@@ -215,9 +262,9 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = lane >> 3, g = lane & 7;
   unsigned char* wbase = ismem + warp * G::kBytes;
-  uint32_t* wsort = reinterpret_cast<uint32_t*>(wbase + G::kRing) + grp * BS;
-  float* wr = reinterpret_cast<float*>(wbase + G::kRing) + 4 * BS + grp * BS;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(wbase + G::kRing + 2 * 4 * BS * 4);
+  uint32_t* wsort = reinterpret_cast<uint32_t*>(wbase + G::kRing) + grp * G::kRow;
+  float* wr = reinterpret_cast<float*>(wbase + G::kRing + G::kArea) + grp * G::kRow;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(wbase + G::kRing + 2 * G::kArea);
 
   const int64_t blocks_per_chunk = (int64_t)G::kTiles * 4;
   const int64_t n_chunks = (p.n_blocks + blocks_per_chunk - 1) / blocks_per_chunk;
@@ -342,6 +389,34 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
                                            : nullptr;
       float best_E = METHOD == kSSE ? E0 : int_hess<BS, FMT, DT>(x, s, rc, s_fin, Hj, wr);
       int best_c = -1;
+      if constexpr (METHOD == kSSE && BS <= 32) {
+        // candidate-parallel: lane g of the group takes candidates lo + 8r + g
+        // over the whole block; the group keeps the lowest (E, code), which is
+        // the first minimum of the ascending scan
+#pragma unroll
+        for (int j = 0; j < NE; ++j) wr[g + 8 * j] = fabsf(x[j]);
+        __syncwarp();
+        const int n_rounds = (int)__reduce_max_sync(0xffffffffu, (unsigned)((n + 7) >> 3));
+        float axr[BS];
+#pragma unroll
+        for (int i = 0; i < BS; ++i) axr[i] = wr[i];
+#pragma unroll 1
+        for (int r = 0; r < n_rounds; ++r) {
+          const int jc = 8 * r + g;
+          const bool act = jc < n;
+          int c = act ? lo + jc : 0;
+          float E = __int_as_float(0x7f800000);
+          if (act) E = lane_row_sse<BS, FMT, DT>(axr, s_itab[c], s_irc[c]);
+#pragma unroll
+          for (int o = 1; o < 8; o <<= 1) {
+            const float E2 = __shfl_xor_sync(0xffffffffu, E, o);
+            const int c2 = __shfl_xor_sync(0xffffffffu, c, o);
+            if (E2 < E || (E2 == E && c2 < c)) { E = E2; c = c2; }
+          }
+          if (E < best_E) { best_E = E; best_c = c; }
+        }
+        __syncwarp();  // wr is rewritten by the next block
+      } else {
 #pragma unroll 1
       for (int it = 0; it < n_max; ++it) {
         const bool act = it < n;
@@ -359,6 +434,7 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
           if (!pass) continue;
         }
         if (act && E < best_E) { best_E = E; best_c = ci; }
+      }
       }
       if (best_c >= 0) {
         s = s_itab[best_c];
