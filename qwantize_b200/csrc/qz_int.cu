@@ -536,6 +536,7 @@ cudaError_t read_device_error_int(unsigned* out, bool clear) {
 cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, int method, int num_sms,
                                 cudaStream_t st) {
   if (fmt == kNVINT4) {
+    if (method != kHessian) return launch_quantize_nvint4(p, dtype, bs, method, num_sms, st);
     if (bs == 16) return launch_int_d<16, kNVINT4>(p, dtype, method, num_sms, st);
     if (bs == 32) return launch_int_d<32, kNVINT4>(p, dtype, method, num_sms, st);
     return cudaErrorInvalidValue;

@@ -21,6 +21,8 @@ struct QuantArgs {
   int n_table;
 };
 
+cudaError_t launch_quantize_nvint4(const QuantArgs& p, int dtype, int bs, int method, int num_sms,
+                                   cudaStream_t st);
 cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, int method, int num_sms,
                                 cudaStream_t st);
 cudaError_t launch_quantize_table(const QuantArgs& p, int dtype, int bs, int method, int num_sms, cudaStream_t st);

@@ -219,19 +219,54 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table
     if (threadIdx.x == 0) t.n = n_table;
     return;
   }
-  if (threadIdx.x == 0) t.n = FMT == kNVFP4 ? 127 : 255;
+  constexpr bool kE4 = FMT == kNVFP4 || FMT == kNVINT4;
+  if (threadIdx.x == 0) t.n = kE4 ? 127 : 255;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    const bool ok = FMT == kNVFP4 ? (i >= 1 && i <= 126) : (i >= 1 && i <= 254);
-    const float v = ok ? (FMT == kNVFP4 ? e4m3_value(i) : pow2f(i - 127)) : 1.0f;
+    const bool ok = kE4 ? (i >= 1 && i <= 126) : (i >= 1 && i <= 254);
+    const float v = ok ? (kE4 ? e4m3_value(i) : pow2f(i - 127)) : 1.0f;
     t.val[i] = v;
-    t.cn[i] = make_uint2(__float_as_uint(__fmul_rn(__frcp_rn(v), kBiasDown)),
+    // NVINT4 rounds with the unbiased RN(1/s); the E2M1 formats with the biased one
+    t.cn[i] = make_uint2(__float_as_uint(FMT == kNVINT4 ? __frcp_rn(v) : __fmul_rn(__frcp_rn(v), kBiasDown)),
                          FMT == kNVFP4 ? (uint32_t)__half_as_ushort(__float2half_rn(-v)) : 0u);
   }
+}
+
+// NVINT4 block SSE on |x| = a (nvint4/reference.py:49-56): 16-bit inputs and a
+// finite s > 0 round a * RN(1/s) (exact except at half-integer ties, which
+// leave the same |d| = s/2 either way; q s is exact, so d is one FMA);
+// otherwise the IEEE quotient, with s = 0 and NaN propagating as in torch.
+template <int BS, int DT>
+__device__ __forceinline__ float int4_sse(const float (&a)[BS], float s, float rc) {
+  const uint32_t sb = __float_as_uint(s);
+  if (DT != kDtF32 && sb > 0u && sb < 0x7f800000u) {
+    uint64_t sq[BS / 2];
+    const uint64_t c2 = pk2(rc, rc), ms2 = pk2(-s, -s);
+#pragma unroll
+    for (int i = 0; i < BS; i += 2) {
+      const uint64_t a2 = pk2(a[i], a[i + 1]);
+      const float2 y = up2(mul2(a2, c2));
+      const uint64_t q2 = pk2(fminf(rintf(y.x), 7.0f), fminf(rintf(y.y), 7.0f));
+      const uint64_t d = fma2(q2, ms2, a2);
+      sq[i / 2] = mul2(d, d);
+    }
+    return sum8_pairs<BS>(sq);
+  }
+  float d2[BS];
+#pragma unroll
+  for (int i = 0; i < BS; ++i) {
+    float q = rintf(__fdiv_rn(a[i], s));
+    q = q > 7.0f ? 7.0f : q;  // keeps NaN
+    const float d = __fsub_rn(a[i], __fmul_rn(q, s));
+    d2[i] = __fmul_rn(d, d);
+  }
+  return sum8<BS>(d2);
 }
 
 // Candidate SSE: the hardware path for 16-bit inputs, IEEE division for fp32.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
+  if constexpr (FMT == kNVINT4) return int4_sse<BS, DT>(a, t.val[code], __uint_as_float(t.cn[code].x));
+  else
   if constexpr (DT != kDtF32 && FMT == kNVFP4) {
     const uint2 e = t.cn[code];
     return block_sse_hw_nv<BS>(a, e.y, __uint_as_float(e.x));
@@ -245,6 +280,10 @@ __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable&
 // the input is 16-bit; s0 = 0 (NVFP4 blocks below 6 * 2^-10) takes the generic one.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
+  if constexpr (FMT == kNVINT4) {
+    const uint32_t sb = __float_as_uint(s);
+    return int4_sse<BS, DT>(a, s, sb > 0u && sb < 0x7f800000u ? __frcp_rn(s) : 0.0f);
+  }
   if constexpr (DT != kDtF32 && FMT != kTable) {
     if (s > 0.0f) return block_sse_hw<BS>(a, s, __fmul_rn(__frcp_rn(s), kBiasDown));
   }
@@ -404,10 +443,11 @@ __device__ __forceinline__ float naive_scale(uint32_t amax_bits) {
     }
     return s_ctab.val[lo];
   }
-  if (is_nan_bits(amax_bits)) return __uint_as_float(FMT == kNVFP4 ? kNvNanBits : kMxNanBits);
+  if (is_nan_bits(amax_bits)) return __uint_as_float(FMT == kMXFP4 ? kMxNanBits : kNvNanBits);
   float amax = __uint_as_float(amax_bits);
-  if (FMT == kNVFP4) {
-    float c = __fdiv_rn(amax, 6.0f);  // (amax / Q_MAX).clamp(min=1e-12)
+  if (FMT == kNVFP4 || FMT == kNVINT4) {
+    // (amax / Q_MAX).clamp(min=1e-12): Q_MAX 6 (nvfp4/reference.py:114), 7 (nvint4/reference.py:76)
+    float c = __fdiv_rn(amax, FMT == kNVINT4 ? 7.0f : 6.0f);
     c = c < 1e-12f ? 1e-12f : c;
     return e4m3_snap_nonneg(c);
   }
@@ -429,7 +469,8 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
     sq[i / 2] = mul2(a2, a2);
   }
   bool noise = sum8_pairs<BS>(sq) <= E0;
-  float s_min = __fdiv_rn(__fsub_rn(amax, __fsqrt_rn(E0)), 6.0f);
+  constexpr float kQ = FMT == kNVINT4 ? 7.0f : 6.0f, kD0 = FMT == kNVINT4 ? 0.5f : 0.25f;
+  float s_min = __fdiv_rn(__fsub_rn(amax, __fsqrt_rn(E0)), kQ);
   s_min = s_min < 0.0f ? 0.0f : s_min;
   uint32_t srt[BS];
 #pragma unroll
@@ -448,12 +489,12 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
   float y = 0.0f;
 #pragma unroll
   for (int i = 0; i < BS; ++i) y = (i == kidx) ? __uint_as_float(srt[i]) : y;
-  float s_max = __fdiv_rn(y, 0.25f);
+  float s_max = __fdiv_rn(y, kD0);
   if (noise || !(s_min <= s_max)) return;
   if (FMT == kTable) {
     lo = table_count_below(s_min, false);
     hi = table_count_below(s_max, true) - 1;
-  } else if (FMT == kNVFP4) {
+  } else if (FMT == kNVFP4 || FMT == kNVINT4) {
     lo = e4m3_ceil_code(s_min);
     hi = e4m3_floor_code(s_max);
   } else {
@@ -602,8 +643,84 @@ __device__ __forceinline__ void write_outputs_hw(const QuantArgs& p, int64_t b, 
   }
 }
 
+// NVINT4 outputs of one block (nvint4/reference.py:29-46): quants =
+// clamp(round(x / s), -7, 7) with round half to even, dequant q * s.  For
+// 16-bit input and a finite s > 0, q = rint(x * RN(1/s)) except at an exact
+// tie |x - q s| == s/2 (q s exact), where an odd q moves to its even
+// neighbour.  Otherwise the IEEE quotient with the reference's x86 NaN
+// payloads: x's NaN, else s's, 0 / 0 the default NaN; the dequant takes the
+// scale's NaN first.  packed: two's complement nibbles, element 2i low, 0x8
+// for a NaN quant; scale code: the E4M3 byte of s.
+template <int BS, int DT>
+__device__ __forceinline__ void write_block_int4(const QuantArgs& p, int64_t b, const float (&x)[BS], float s) {
+  const uint32_t sb = __float_as_uint(s);
+  const bool fast = DT != kDtF32 && sb > 0u && sb < 0x7f800000u;
+  const bool snan = is_nan_bits(sb & 0x7fffffffu);
+  const float rc = fast ? __frcp_rn(s) : 0.0f;
+  uint32_t words[BS / 8];
+#pragma unroll
+  for (int w = 0; w < BS / 8; ++w) {  // eight elements per step, stored as 16-byte vectors
+    float q8[8], d8[8];
+    uint32_t word = 0u;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float xv = x[8 * w + k];
+      float q;
+      if (fast) {
+        q = rintf(__fmul_rn(xv, rc));
+        if (fabsf(q) <= 8.0f) {
+          const float e = __fmaf_rn(-q, s, xv);
+          if (fabsf(e) == __fmul_rn(0.5f, s) && (__float2int_rz(q) & 1)) q = __fadd_rn(q, e > 0.0f ? 1.0f : -1.0f);
+        }
+        q = fminf(fmaxf(q, -7.0f), 7.0f);  // keeps -0.0
+      } else {
+        const uint32_t xb = __float_as_uint(xv);
+        if (is_nan_bits(xb & 0x7fffffffu)) q = __uint_as_float(xb | 0x00400000u);
+        else if (snan) q = s;
+        else if (s == 0.0f && xv == 0.0f) q = __uint_as_float(0xffc00000u);
+        else {
+          q = rintf(__fdiv_rn(xv, s));
+          q = q < -7.0f ? -7.0f : (q > 7.0f ? 7.0f : q);
+        }
+      }
+      const bool qn = is_nan_bits(__float_as_uint(q) & 0x7fffffffu);
+      q8[k] = q;
+      d8[k] = snan ? s : (qn ? q : __fmul_rn(q, s));
+      word |= (qn ? 0x8u : ((uint32_t)__float2int_rn(q) & 0xfu)) << (4 * k);
+    }
+    words[w] = word;
+    if (p.dq_bf16) {  // exact: the dequant has <= 7 significant bits
+      uint32_t h[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        h[k] = (__float_as_uint(d8[2 * k]) >> 16) | (__float_as_uint(d8[2 * k + 1]) & 0xffff0000u);
+      reinterpret_cast<uint4*>(p.dq_bf16 + b * BS)[w] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    if (p.quants) {
+      float4* o = reinterpret_cast<float4*>(p.quants + b * BS + 8 * w);
+      o[0] = make_float4(q8[0], q8[1], q8[2], q8[3]);
+      o[1] = make_float4(q8[4], q8[5], q8[6], q8[7]);
+    }
+    if (p.dq) {
+      float4* o = reinterpret_cast<float4*>(p.dq + b * BS + 8 * w);
+      o[0] = make_float4(d8[0], d8[1], d8[2], d8[3]);
+      o[1] = make_float4(d8[4], d8[5], d8[6], d8[7]);
+    }
+  }
+  if (p.scales) p.scales[b] = s;
+  if (p.scale_codes) p.scale_codes[b] = (uint8_t)e4m3_code(s);
+  if (p.packed) {
+    if constexpr (BS == 16) *reinterpret_cast<uint2*>(p.packed + b * 8) = make_uint2(words[0], words[1]);
+    else *reinterpret_cast<uint4*>(p.packed + b * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+  }
+}
+
 template <int BS, int FMT, int METHOD, int DT>
 __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const float (&x)[BS], float s) {
+  if constexpr (FMT == kNVINT4) {
+    write_block_int4<BS, DT>(p, b, x, s);
+    return;
+  }
   constexpr int MODE = Mode<FMT, DT>::v;
   float quant[BS];
   uint32_t nib[BS];
@@ -771,7 +888,7 @@ struct WarpGeom {
 // Minimum resident CTAs per SM (register caps), chosen by measurement.
 template <int BS, int FMT, int METHOD>
 struct MinCtas {
-  static constexpr int v = METHOD != kSSE ? 1 : (BS == 16 ? (FMT == kNVFP4 ? 3 : 4) : 2);
+  static constexpr int v = METHOD != kSSE ? 1 : (BS == 16 ? ((FMT == kNVFP4 || FMT == kNVINT4) ? 3 : 4) : 2);
 };
 
 // Naive / SSE / argmin methods.
@@ -1221,6 +1338,29 @@ cudaError_t launch_quantize_table(const QuantArgs& p, int dtype, int bs, int met
   if (p.n_blocks == 0) return cudaSuccess;
   return bs == 16 ? launch_fmt<16, kTable>(p, dtype, method, num_sms, st)
                   : launch_fmt<32, kTable>(p, dtype, method, num_sms, st);
+}
+
+// NVINT4 naive / SSE on the per-thread-block kernel (the Hessian variant and
+// INT8 run in qz_int.cu).
+template <int BS>
+static cudaError_t launch_nvint4_bs(const QuantArgs& p, int dtype, int method, int sms, cudaStream_t st) {
+  if (method == kNaive) {
+    if (dtype == kDtBF16) return launch_q<BS, kNVINT4, kNaive, kDtBF16>(p, sms, st);
+    if (dtype == kDtF16) return launch_q<BS, kNVINT4, kNaive, kDtF16>(p, sms, st);
+    return launch_q<BS, kNVINT4, kNaive, kDtF32>(p, sms, st);
+  }
+  if (method == kSSE) {
+    if (dtype == kDtBF16) return launch_q<BS, kNVINT4, kSSE, kDtBF16>(p, sms, st);
+    if (dtype == kDtF16) return launch_q<BS, kNVINT4, kSSE, kDtF16>(p, sms, st);
+    return launch_q<BS, kNVINT4, kSSE, kDtF32>(p, sms, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_quantize_nvint4(const QuantArgs& p, int dtype, int bs, int method, int num_sms, cudaStream_t st) {
+  if (p.n_blocks == 0) return cudaSuccess;
+  return bs == 16 ? launch_nvint4_bs<16>(p, dtype, method, num_sms, st)
+                  : launch_nvint4_bs<32>(p, dtype, method, num_sms, st);
 }
 
 cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int method,
