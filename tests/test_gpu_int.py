@@ -167,3 +167,21 @@ def test_int_full_config_digests(name, fmt, bs):
         ref = d[f"{name}_{method}_{bs}"]
         for t, k in ((s, "scales"), (qq, "quants"), (dq, "dq")):
             assert hashlib.sha256(t.cpu().numpy().tobytes()).hexdigest() == ref[k], (method, k)
+
+
+@pytest.mark.parametrize("name,bs", [("nvint4", 16), ("int8", 64)])
+def test_int_dim0_and_cpu_input(name, bs):
+    """Block dimension first (dim=0) gives the same per-block results as the
+    default layout; a CPU input returns CPU tensors with the same values."""
+    from qwantize_b200.synthetic import make_weight
+    mod = _mod(name)
+    W = make_weight(24, 4 * bs, seed=5).reshape(24, 4, bs)
+    s, qq, dq = getattr(mod, f"{name}_optimal")(W.to(DEV), return_dequant=True)
+    Wt = W.permute(2, 0, 1).contiguous()  # (bs, 24, 4)
+    st, qt, dqt = getattr(mod, f"{name}_optimal")(Wt.to(DEV), dim=0, return_dequant=True)
+    assert st.shape == (24, 4) and qt.shape == Wt.shape
+    assert same_bits(st.cpu().numpy(), s.cpu().numpy())
+    assert same_bits(qt.permute(1, 2, 0).cpu().numpy(), qq.cpu().numpy())
+    sc, qc = getattr(mod, f"{name}_optimal")(W)
+    assert sc.device.type == "cpu" and qc.device.type == "cpu"
+    assert same_bits(sc.numpy(), s.cpu().numpy()) and same_bits(qc.numpy(), qq.cpu().numpy())
