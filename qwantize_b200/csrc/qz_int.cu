@@ -240,7 +240,7 @@ struct IGeom {
   static constexpr int kTile = 4 * BS * Elem<DT>::kSize;
   static constexpr int kTiles = kTile >= 2048 ? 1 : 2048 / kTile;
   static constexpr int kStage = kTiles * kTile;
-  static constexpr int kStages = kStage <= 2048 ? 4 : 2;
+  static constexpr int kStages = kStage < 2048 ? 4 : 2;  // two for 2 KB stages: two CTAs per SM at bs 256
   static constexpr int kRing = kStages * kStage;
   static constexpr int kRow = BS + 4;  // padded per-group row (floats): no bank conflicts across groups
   static constexpr int kArea = 4 * kRow * 4;
