@@ -305,10 +305,11 @@ def bench_ours(args):
 
     extra = None
     if not args.no_extras:
-        peak_tf = 1657.2
+        peak_tf = (1590.0, 1400.0)  # fallback (burst, sustained) when the measured file is absent
         try:
             with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                peak_tf = json.load(f).get("bf16_tflops", peak_tf)
+                pk = json.load(f)
+                peak_tf = (pk.get("bf16_tflops", peak_tf[0]), pk.get("bf16_tflops_sustained", peak_tf[1]))
         except OSError:
             pass
         del pool
@@ -409,7 +410,9 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
     out["config2_gram"] = {
         "tokens": T, "K": Kx, "ms_full": ms_full, "tflops_full_whole_job": flop / ms_full / 1e9,
         "tflops_full_per_gpu": flop / ms_full / 1e9 / ws,
-        "frac_of_measured_bf16_peak": flop / ms_full / 1e9 / ws / peak_tf,
+        # a ~100 ms kernel runs under the power cap: the sustained peak is its denominator
+        "frac_of_measured_bf16_peak_sustained": flop / ms_full / 1e9 / ws / peak_tf[1],
+        "frac_of_measured_bf16_peak_burst": flop / ms_full / 1e9 / ws / peak_tf[0],
         "ms_blockdiag": ms_diag, "blockdiag_GBps": 2 * (t1 - t0) * Kx / ms_diag / 1e6,
         "allreduce_full_H_ms": ar_ms, "sharding": f"tokens over {ws} rank(s), whole 65536-token chunks"}
     W = make_weight_device(2560, Kx, 0, device)
@@ -431,7 +434,8 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         "weights": 2560 * Kx, "nvfp4_bs16_search_ms": ms_nv, "mxfp4_bs16_search_ms": ms_mx,
         "nvfp4_admm_bs16_ms": ms_admm,
         "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
-        "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9}
+        "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9,
+        "metrics_frac_of_measured_bf16_peak_sustained": mflop / ms_m / 1e9 / peak_tf[1]}
     # NVINT4 / INT8 on the config-1 weight (native outputs: scale bytes, packed codes, bf16 dequant)
     Lq = _lib.load()
     n_w = 2560 * Kx
