@@ -1,6 +1,9 @@
-// qz_int.cu -- NVINT4 and INT8 block quantization: the symmetric integer grids
-// of nvint4/reference.py and int8/reference.py on the same search skeleton as
-// NVFP4 (naive scale, SSE bounds, bounded exhaustive search, Hessian variant).
+// qz_int.cu -- INT8 block quantization (int8/reference.py; blocks of 32 to 256):
+// the symmetric integer grid on the same search skeleton as NVFP4 (naive scale,
+// SSE bounds, bounded exhaustive search, Hessian variant).  NVINT4, whose
+// blocks of 16 / 32 fit one lane, runs on the per-thread-block kernels of
+// qz_quantize.cu; the code here keeps its NVINT4 arithmetic for reference
+// but launches INT8 only.
 //
 //   quants = clamp(round(x / s), -Q, Q)   (round half to even)
 //   NVINT4: Q = 7,   s = e4m3(max(amax / 7, 1e-12)),  bs 16 / 32, candidates: E4M3
@@ -536,10 +539,7 @@ cudaError_t read_device_error_int(unsigned* out, bool clear) {
 cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, int method, int num_sms,
                                 cudaStream_t st) {
   if (fmt == kNVINT4) {
-    if (method != kHessian) return launch_quantize_nvint4(p, dtype, bs, method, num_sms, st);
-    if (bs == 16) return launch_int_d<16, kNVINT4>(p, dtype, method, num_sms, st);
-    if (bs == 32) return launch_int_d<32, kNVINT4>(p, dtype, method, num_sms, st);
-    return cudaErrorInvalidValue;
+    return launch_quantize_nvint4(p, dtype, bs, method, num_sms, st);  // qz_quantize.cu
   }
   if (fmt == kInt8) {
     switch (bs) {

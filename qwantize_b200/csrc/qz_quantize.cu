@@ -231,6 +231,29 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table
   }
 }
 
+// clamp(round(x / s), -7, 7), round half to even (int4_quantize,
+// nvint4/reference.py:29-41).  fast (16-bit input, finite s > 0, rc = RN(1/s)):
+// rint(x * rc), exact except at a tie |x - q s| == s/2 (q s exact), where an
+// odd q moves to its even neighbour.  Otherwise the IEEE quotient with the
+// reference's x86 NaN payloads: x's NaN, else s's, 0 / 0 the default NaN.
+__device__ __forceinline__ float int4_q(float xv, float s, float rc, bool fast, bool snan) {
+  float q;
+  if (fast) {
+    q = rintf(__fmul_rn(xv, rc));
+    if (fabsf(q) <= 8.0f) {
+      const float e = __fmaf_rn(-q, s, xv);
+      if (fabsf(e) == __fmul_rn(0.5f, s) && (__float2int_rz(q) & 1)) q = __fadd_rn(q, e > 0.0f ? 1.0f : -1.0f);
+    }
+    return fminf(fmaxf(q, -7.0f), 7.0f);  // keeps -0.0
+  }
+  const uint32_t xb = __float_as_uint(xv);
+  if (is_nan_bits(xb & 0x7fffffffu)) return __uint_as_float(xb | 0x00400000u);
+  if (snan) return s;
+  if (s == 0.0f && xv == 0.0f) return __uint_as_float(0xffc00000u);
+  q = rintf(__fdiv_rn(xv, s));
+  return q < -7.0f ? -7.0f : (q > 7.0f ? 7.0f : q);
+}
+
 // NVINT4 block SSE on |x| = a (nvint4/reference.py:49-56): 16-bit inputs and a
 // finite s > 0 round a * RN(1/s) (exact except at half-integer ties, which
 // leave the same |d| = s/2 either way; q s is exact, so d is one FMA);
@@ -290,10 +313,11 @@ __device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
   return block_sse<BS, MODE>(a, s);
 }
 
-// Clipping error sum(clamp(|x| - 6 s, 0)^2) (nvfp4/reference.py:209).
-template <int BS>
+// Clipping error sum(clamp(|x| - Q s, 0)^2) (nvfp4/reference.py:209; Q = 7 for
+// NVINT4, nvint4/reference.py:258).
+template <int BS, int FMT = kNVFP4>
 __device__ __forceinline__ float block_clip(const float (&a)[BS], float s) {
-  float t = __fmul_rn(6.0f, s), v[BS];
+  float t = __fmul_rn(FMT == kNVINT4 ? 7.0f : 6.0f, s), v[BS];
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
     float c = __fsub_rn(a[i], t);
@@ -362,11 +386,21 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
 // uses the hardware rounding: r = x - sign(x) q s = +-RN(|x| - q s) with the
 // sign of x applied by flipping the sign bit, bit-identical to the generic path
 // (q s is exact).
-template <int BS, int MODE, int DT>
+template <int BS, int MODE, int DT, int FMT = kNVFP4>
 __device__ __forceinline__ float block_hess_ilp(const float (&x)[BS], const float (&a)[BS], float s,
                                                 const float* __restrict__ Ht) {
   float r[BS];
-  if (MODE != kDiv && s > 0.0f) {  // 16-bit input with an E4M3 / UE8M0 scale
+  if constexpr (FMT == kNVINT4) {  // r = x - dq with the exact int4 rounding (dq: the scale's NaN first)
+    const uint32_t sb = __float_as_uint(s);
+    const bool fast = DT != kDtF32 && sb > 0u && sb < 0x7f800000u, snan = is_nan_bits(sb & 0x7fffffffu);
+    const float rc = fast ? __frcp_rn(s) : 0.0f;
+#pragma unroll
+    for (int i = 0; i < BS; ++i) {
+      const float q = int4_q(x[i], s, rc, fast, snan);
+      const float dq = snan ? s : (is_nan_bits(__float_as_uint(q) & 0x7fffffffu) ? q : __fmul_rn(q, s));
+      r[i] = __fsub_rn(x[i], dq);
+    }
+  } else if (MODE != kDiv && s > 0.0f) {  // 16-bit input with an E4M3 / UE8M0 scale
     const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
 #pragma unroll
     for (int i = 0; i < BS; i += 2) {
@@ -509,7 +543,7 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
 template <int FMT>
 __device__ __forceinline__ float cand_value(int c) {
   if constexpr (FMT == kTable) return s_ctab.val[c];
-  return FMT == kNVFP4 ? e4m3_value(c) : pow2f(c - 127);
+  return (FMT == kNVFP4 || FMT == kNVINT4) ? e4m3_value(c) : pow2f(c - 127);
 }
 
 // Signed codebook of mxfp4/kernels.py:284-287 (entry 8 is +0.0).
@@ -664,25 +698,7 @@ __device__ __forceinline__ void write_block_int4(const QuantArgs& p, int64_t b, 
     uint32_t word = 0u;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float xv = x[8 * w + k];
-      float q;
-      if (fast) {
-        q = rintf(__fmul_rn(xv, rc));
-        if (fabsf(q) <= 8.0f) {
-          const float e = __fmaf_rn(-q, s, xv);
-          if (fabsf(e) == __fmul_rn(0.5f, s) && (__float2int_rz(q) & 1)) q = __fadd_rn(q, e > 0.0f ? 1.0f : -1.0f);
-        }
-        q = fminf(fmaxf(q, -7.0f), 7.0f);  // keeps -0.0
-      } else {
-        const uint32_t xb = __float_as_uint(xv);
-        if (is_nan_bits(xb & 0x7fffffffu)) q = __uint_as_float(xb | 0x00400000u);
-        else if (snan) q = s;
-        else if (s == 0.0f && xv == 0.0f) q = __uint_as_float(0xffc00000u);
-        else {
-          q = rintf(__fdiv_rn(xv, s));
-          q = q < -7.0f ? -7.0f : (q > 7.0f ? 7.0f : q);
-        }
-      }
+      const float q = int4_q(x[8 * w + k], s, rc, fast, snan);
       const bool qn = is_nan_bits(__float_as_uint(q) & 0x7fffffffu);
       q8[k] = q;
       d8[k] = snan ? s : (qn ? q : __fmul_rn(q, s));
@@ -1085,19 +1101,19 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
     float s = naive_scale<FMT>(amax_bits);
     if (!is_nan_bits(__float_as_uint(s) & 0x7fffffffu)) {
       const float E0 = base_sse<BS, MODE, DT, FMT>(a, s);
-      float best_E = block_hess_ilp<BS, MODE, DT>(x, a, s, Ht);
+      float best_E = block_hess_ilp<BS, MODE, DT, FMT>(x, a, s, Ht);
       int lo, hi;
       search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
 #pragma unroll 1
       for (int c = lo; c <= hi; ++c) {
         const float sc = cand_value<FMT>(c);
-        const float Hc = block_clip<BS>(a, sc);
+        const float Hc = block_clip<BS, FMT>(a, sc);
         // NVFP4 fast-fail: 10x the running Hessian best (nvfp4/reference.py:377);
         // MXFP4: the baseline SSE (mxfp4/reference.py:346).
         // (the exotic-grid experiment uses the NVFP4 rule: quant_exotic_scales.py:157)
         const bool pass = FMT != kMXFP4 ? (Hc < __fmul_rn(best_E, 10.0f)) : (Hc < E0);
         if (!pass) continue;
-        const float E = block_hess_ilp<BS, MODE, DT>(x, a, sc, Ht);
+        const float E = block_hess_ilp<BS, MODE, DT, FMT>(x, a, sc, Ht);
         if (E < best_E) { best_E = E; s = sc; }
       }
     }
@@ -1340,10 +1356,27 @@ cudaError_t launch_quantize_table(const QuantArgs& p, int dtype, int bs, int met
                   : launch_fmt<32, kTable>(p, dtype, method, num_sms, st);
 }
 
-// NVINT4 naive / SSE on the per-thread-block kernel (the Hessian variant and
-// INT8 run in qz_int.cu).
+template <int BS, int DT>
+static cudaError_t launch_hessian_nvint4(const QuantArgs& p, int num_sms, cudaStream_t st) {
+  const int64_t M = p.n_blocks / p.n_col_blocks;
+  int64_t gy = (M + 127) / 128;
+  const int64_t want = (int64_t)num_sms * 16;
+  const int64_t per_j = (want + p.n_col_blocks - 1) / p.n_col_blocks;
+  gy = gy < per_j ? gy : per_j;
+  if (gy < 1) gy = 1;
+  if (gy > 65535) gy = 65535;
+  hessian_kernel<BS, kNVINT4, DT><<<dim3((unsigned)p.n_col_blocks, (unsigned)gy), 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+// NVINT4 on the per-thread-block kernels (INT8 runs in qz_int.cu).
 template <int BS>
 static cudaError_t launch_nvint4_bs(const QuantArgs& p, int dtype, int method, int sms, cudaStream_t st) {
+  if (method == kHessian) {
+    if (dtype == kDtBF16) return launch_hessian_nvint4<BS, kDtBF16>(p, sms, st);
+    if (dtype == kDtF16) return launch_hessian_nvint4<BS, kDtF16>(p, sms, st);
+    return launch_hessian_nvint4<BS, kDtF32>(p, sms, st);
+  }
   if (method == kNaive) {
     if (dtype == kDtBF16) return launch_q<BS, kNVINT4, kNaive, kDtBF16>(p, sms, st);
     if (dtype == kDtF16) return launch_q<BS, kNVINT4, kNaive, kDtF16>(p, sms, st);
