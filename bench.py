@@ -420,8 +420,23 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
     X = make_activations(t1 - t0, Kx, seed=1, device=device, t0=t0)
     H = torch.empty(Kx, Kx, device=device)
     Hb = torch.empty(Kx // 16, 16, 16, device=device)
-    ms_full = _max_over_ranks(_ev_time(lambda: gram(X, "full", out=H), stream), ws, device)
+    # the block-diagonal Gram (HBM-bound) first, before the ~100 ms full Gram drives the clocks down
     ms_diag = _max_over_ranks(_ev_time(lambda: gram(X, "blockdiag", 16, out=Hb), stream, 3), ws, device)
+    W = make_weight_device(2560, Kx, 0, device)
+    Wb = W.reshape(2560, Kx // 16, 16)
+    # the searches need only the block diagonal: timed before the full Gram as well
+    Hbd = Hb  # the search uses the block diagonal, all-reduced over ranks when N > 1
+    if ws > 1:
+        torch.distributed.all_reduce(Hbd)
+    ms_nv = _ev_time(lambda: q.nvfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    ms_mx = _ev_time(lambda: q.mxfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    out["config1_int_formats"]["nvint4_hoptimal_bs16_search_ms"] = _ev_time(
+        lambda: q.nvint4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
+    from qwantize_b200.core import admm_fp32
+    from qwantize_b200.hessian import admm_setup
+    Hn, Minv = admm_setup(Hbd)
+    ms_admm = _ev_time(lambda: admm_fp32(Wb, -1, False, Hbd, Hn, Minv), stream, 3)
+    ms_full = _max_over_ranks(_ev_time(lambda: gram(X, "full", out=H), stream), ws, device)
     ar_ms = None
     if ws > 1:
         torch.distributed.barrier()
@@ -435,17 +450,6 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         "frac_of_measured_bf16_peak_burst": flop / ms_full / 1e9 / ws / peak_tf[0],
         "ms_blockdiag": ms_diag, "blockdiag_GBps": 2 * (t1 - t0) * Kx / ms_diag / 1e6,
         "allreduce_full_H_ms": ar_ms, "sharding": f"tokens over {ws} rank(s), whole 65536-token chunks"}
-    W = make_weight_device(2560, Kx, 0, device)
-    Wb = W.reshape(2560, Kx // 16, 16)
-    Hbd = Hb  # the search uses the block diagonal, all-reduced over ranks when N > 1
-    if ws > 1:
-        torch.distributed.all_reduce(Hbd)
-    ms_nv = _ev_time(lambda: q.nvfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
-    ms_mx = _ev_time(lambda: q.mxfp4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
-    from qwantize_b200.core import admm_fp32
-    from qwantize_b200.hessian import admm_setup
-    Hn, Minv = admm_setup(Hbd)
-    ms_admm = _ev_time(lambda: admm_fp32(Wb, -1, False, Hbd, Hn, Minv), stream, 3)
     _, _, dq = q.nvfp4_optimal(Wb, return_dequant=True)
     dqb = dq.reshape(2560, Kx).to(torch.bfloat16)
     ms_m = _max_over_ranks(_ev_time(lambda: output_error_sums(W, dqb, X), stream), ws, device)
@@ -456,8 +460,6 @@ def extras(ws, rank, device, peak_tf, T=1048576, n_layers=36):
         "nvfp4_hopt_gweights_per_s_incl_blockdiag_gram": 2560 * Kx / ((ms_nv + ms_diag) / 1e3) / 1e9,
         "metrics_output_error_ms": ms_m, "metrics_tflops_per_gpu": mflop / ms_m / 1e9,
         "metrics_frac_of_measured_bf16_peak_sustained": mflop / ms_m / 1e9 / peak_tf[1]}
-    out["config1_int_formats"]["nvint4_hoptimal_bs16_search_ms"] = _ev_time(
-        lambda: q.nvint4_optimal_hessian(Wb, H_blocks=Hbd), stream, 3)
     # GPTQ (NVFP4 bs16 SSE-optimal) of the 2560x9728 weight on the full H / T
     from qwantize_b200.gptq import gptq
     H.div_(T)
