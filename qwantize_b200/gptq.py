@@ -76,8 +76,11 @@ def gptq(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "op
     # column-block-major working copy: Wb[j] is W[:, j*bs:(j+1)*bs]
     Wb = W.float().reshape(M, nblk, bs).permute(1, 0, 2).contiguous()
     Qb = torch.empty_like(Wb)
-    loss = torch.zeros((), dtype=torch.float64, device=dev)
     gb = max(1, group // bs)  # column blocks per lazy-batch group
+    # few host-issued launches per column block: the loop is bound by issue rate
+    h_diag_all = Hi.diagonal().contiguous().reshape(nblk, bs)
+    parts = torch.empty(nblk, dtype=torch.float64, device=dev)  # per-block loss, summed once
+    d = torch.empty(M, bs, dtype=torch.float32, device=dev)
     for g0 in range(0, nblk, gb):
         g1 = min(nblk, g0 + gb)
         Eg = torch.empty(g1 - g0, M, bs, dtype=torch.float32, device=dev)  # scaled errors of the group
@@ -85,21 +88,20 @@ def gptq(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "op
             w_blk = Wb[j]
             q = _quant_block(w_blk, bs, fmt_c, meth_c, H_blocks[j] if H_blocks is not None else None, Qb[j])
             cs = j * bs
-            h_diag = Hi.diagonal()[cs:cs + bs]
-            d = w_blk - q
-            err = d / h_diag
-            loss += (d * d / h_diag).sum(dtype=torch.float64)
-            Eg[j - g0] = err
+            torch.sub(w_blk, q, out=d)
+            err = torch.div(d, h_diag_all[j], out=Eg[j - g0])
+            torch.sum(d * err, dim=(0, 1), dtype=torch.float64, out=parts[j])  # d^2 / h_jj
             if j + 1 < g1:  # update the rest of the group: W[:, ce:g_end] -= err @ Hi[cs:ce, ce:g_end]
-                h_cross = Hi[cs:cs + bs, (j + 1) * bs:g1 * bs].reshape(bs, g1 - j - 1, bs)
-                Wb[j + 1:g1] -= torch.einsum("mi,ijc->jmc", err, h_cross)
+                rest = g1 - j - 1
+                upd = torch.mm(err, Hi[cs:cs + bs, (j + 1) * bs:g1 * bs])  # (M, rest * bs)
+                Wb[j + 1:g1] -= upd.view(M, rest, bs).transpose(0, 1)
         if g1 < nblk:  # everything after the group at once
             rows = Hi[g0 * bs:g1 * bs, g1 * bs:]  # (group cols, rest)
             E2 = Eg.permute(1, 0, 2).reshape(M, (g1 - g0) * bs)
             upd = E2 @ rows  # (M, rest)
             Wb[g1:] -= upd.reshape(M, nblk - g1, bs).permute(1, 0, 2)
     Q = Qb.permute(1, 0, 2).reshape(M, K)
-    return Q, float(loss.item()) / M
+    return Q, float(parts.sum().item()) / M
 
 
 def gptq_ordered(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "optimal",
