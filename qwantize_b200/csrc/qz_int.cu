@@ -123,10 +123,11 @@ __device__ __forceinline__ float int_sse(const float (&x)[BS / 8], float s, floa
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < BS / 8; ++j) {
-      const float q = rintf(__fdiv_rn(x[j], s));
-      const float qc = q < -IntQ<FMT>::v ? -IntQ<FMT>::v : (q > IntQ<FMT>::v ? IntQ<FMT>::v : q);
-      const float d = __fsub_rn(x[j], __fmul_rn(qc, s));
+    for (int j = 0; j < BS / 8; ++j) {  // on |x| (the SSE is sign-symmetric); NaN propagates
+      const float a = fabsf(x[j]);
+      const float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
+      const float qc = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
+      const float d = __fsub_rn(a, __fmul_rn(qc, s));
       d2[j] = __fmul_rn(d, d);
     }
   }
@@ -141,7 +142,9 @@ __device__ __forceinline__ float int_d2(float a, float s, float rc) {
     const float q = fminf(rintf(__fmul_rn(a, rc)), 7.0f);
     d = __fmaf_rn(-q, s, a);
   } else {
-    float q = rintf(__fdiv_rn(a, s));
+    // rint of a / s >= 0 on the FMA pipe: (y + 1.5*2^23) - 1.5*2^23 is round
+    // half to even below 2^22, and above it still clamps to Q
+    float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
     q = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
     d = __fsub_rn(a, __fmul_rn(q, s));
   }

@@ -264,11 +264,14 @@ __device__ __forceinline__ float int4_sse(const float (&a)[BS], float s, float r
   if (DT != kDtF32 && sb > 0u && sb < 0x7f800000u) {
     uint64_t sq[BS / 2];
     const uint64_t c2 = pk2(rc, rc), ms2 = pk2(-s, -s);
+    const uint64_t kMagic2 = pk2(12582912.0f, 12582912.0f), kNegMagic2 = pk2(-12582912.0f, -12582912.0f);
 #pragma unroll
     for (int i = 0; i < BS; i += 2) {
       const uint64_t a2 = pk2(a[i], a[i + 1]);
-      const float2 y = up2(mul2(a2, c2));
-      const uint64_t q2 = pk2(fminf(rintf(y.x), 7.0f), fminf(rintf(y.y), 7.0f));
+      // round half to even of y >= 0 on the FMA pipe: (y + 1.5*2^23) - 1.5*2^23
+      // (exact below 2^22; above it the result still clamps to 7)
+      const float2 y = up2(add2(add2(mul2(a2, c2), kMagic2), kNegMagic2));
+      const uint64_t q2 = pk2(fminf(y.x, 7.0f), fminf(y.y, 7.0f));
       const uint64_t d = fma2(q2, ms2, a2);
       sq[i / 2] = mul2(d, d);
     }
