@@ -111,9 +111,8 @@ static int quantize_int(const void* x, int x_dtype, int64_t n_blocks, int block_
   if (n_blocks < 0) return fail(QZ_ERR_INVALID, "n_blocks must be >= 0");
   if (n_blocks == 0) return QZ_OK;
   if (!x || !aligned(x, 16)) return fail(QZ_ERR_INVALID, "x must be non-NULL and 16-byte aligned");
-  if (format == QZ_FMT_NVINT4 &&
-      ((quants && !aligned(quants, 16)) || (dq && !aligned(dq, 16)) || (dq_bf16 && !aligned(dq_bf16, 16)) ||
-       (packed && !aligned(packed, block_size == 16 ? 8 : 16))))
+  if ((quants && !aligned(quants, 16)) || (dq && !aligned(dq, 16)) || (dq_bf16 && !aligned(dq_bf16, 16)) ||
+      (packed && !aligned(packed, format == QZ_FMT_NVINT4 && block_size == 16 ? 8 : 16)))
     return fail(QZ_ERR_INVALID, "quants/dq/dq_bf16 must be 16-byte aligned, packed 8/16-byte aligned");
   if ((quants && !aligned(quants, 4)) || (dq && !aligned(dq, 4)) || (dq_bf16 && !aligned(dq_bf16, 2)))
     return fail(QZ_ERR_INVALID, "quants/dq must be 4-byte aligned, dq_bf16 2-byte aligned");

@@ -23,6 +23,7 @@ struct QuantArgs {
 
 cudaError_t launch_quantize_nvint4(const QuantArgs& p, int dtype, int bs, int method, int num_sms,
                                    cudaStream_t st);
+cudaError_t launch_quantize_int8_bs32(const QuantArgs& p, int dtype, int method, int num_sms, cudaStream_t st);
 cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, int method, int num_sms,
                                 cudaStream_t st);
 cudaError_t launch_quantize_table(const QuantArgs& p, int dtype, int bs, int method, int num_sms, cudaStream_t st);

@@ -26,6 +26,8 @@
 //   argmin  mxfp4/kernels.py:267-377 (mxfp4_naive_torch / mxfp4_optimal_torch)
 // Compiled with -fmad=false: every product and sum is separately rounded, in
 // the order torch's CPU kernels use, so results are bit-identical.
+#include <cuda_bf16.h>
+
 #include "qz_common.cuh"
 #include "qz_kernels.h"
 #include "qz_ptx.cuh"
@@ -219,6 +221,17 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table
     if (threadIdx.x == 0) t.n = n_table;
     return;
   }
+  if constexpr (FMT == kInt8) {
+    // int8/reference.py:151-152: the effective scales E4M3 / 127, indexed by E4M3 code
+    // (index 0: scale 0, never a candidate)
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+      const float v = i == 0 ? 0.0f : (i <= 126 ? __fdiv_rn(e4m3_value(i), 127.0f) : 3.0e38f);
+      t.val[i] = v;
+      t.cn[i] = make_uint2(0u, 0u);
+    }
+    if (threadIdx.x == 0) t.n = 127;
+    return;
+  }
   constexpr bool kE4 = FMT == kNVFP4 || FMT == kNVINT4;
   if (threadIdx.x == 0) t.n = kE4 ? 127 : 255;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
@@ -288,10 +301,28 @@ __device__ __forceinline__ float int4_sse(const float (&a)[BS], float s, float r
   return sum8<BS>(d2);
 }
 
+// INT8 block SSE on |x| = a (int8/reference.py:65-83): q = round(a / s) by IEEE
+// division (the scales E4M3 / 127 carry full fp32 mantissas), rounded half to
+// even by the 1.5 * 2^23 add / subtract, clamped to 127 (NaN propagates);
+// d = a - fl(q s) rounds twice, as in the reference.
+template <int BS>
+__device__ __forceinline__ float int8_sse(const float (&a)[BS], float s) {
+  float d2[BS];
+#pragma unroll
+  for (int i = 0; i < BS; ++i) {
+    float q = __fadd_rn(__fadd_rn(__fdiv_rn(a[i], s), 12582912.0f), -12582912.0f);
+    q = q > 127.0f ? 127.0f : q;
+    const float d = __fsub_rn(a[i], __fmul_rn(q, s));
+    d2[i] = __fmul_rn(d, d);
+  }
+  return sum8<BS>(d2);
+}
+
 // Candidate SSE: the hardware path for 16-bit inputs, IEEE division for fp32.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
   if constexpr (FMT == kNVINT4) return int4_sse<BS, DT>(a, t.val[code], __uint_as_float(t.cn[code].x));
+  else if constexpr (FMT == kInt8) return int8_sse<BS>(a, t.val[code]);
   else
   if constexpr (DT != kDtF32 && FMT == kNVFP4) {
     const uint2 e = t.cn[code];
@@ -306,6 +337,7 @@ __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable&
 // the input is 16-bit; s0 = 0 (NVFP4 blocks below 6 * 2^-10) takes the generic one.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
+  if constexpr (FMT == kInt8) return int8_sse<BS>(a, s);
   if constexpr (FMT == kNVINT4) {
     const uint32_t sb = __float_as_uint(s);
     return int4_sse<BS, DT>(a, s, sb > 0u && sb < 0x7f800000u ? __frcp_rn(s) : 0.0f);
@@ -482,6 +514,10 @@ __device__ __forceinline__ float naive_scale(uint32_t amax_bits) {
   }
   if (is_nan_bits(amax_bits)) return __uint_as_float(FMT == kMXFP4 ? kMxNanBits : kNvNanBits);
   float amax = __uint_as_float(amax_bits);
+  if constexpr (FMT == kInt8) {  // e4m3(max(amax, 1e-12)) / 127 (int8/reference.py:112-114)
+    const float v = e4m3_snap_nonneg(amax < 1e-12f ? 1e-12f : amax);
+    return is_nan_bits(__float_as_uint(v)) ? v : __fdiv_rn(v, 127.0f);
+  }
   if (FMT == kNVFP4 || FMT == kNVINT4) {
     // (amax / Q_MAX).clamp(min=1e-12): Q_MAX 6 (nvfp4/reference.py:114), 7 (nvint4/reference.py:76)
     float c = __fdiv_rn(amax, FMT == kNVINT4 ? 7.0f : 6.0f);
@@ -506,7 +542,8 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
     sq[i / 2] = mul2(a2, a2);
   }
   bool noise = sum8_pairs<BS>(sq) <= E0;
-  constexpr float kQ = FMT == kNVINT4 ? 7.0f : 6.0f, kD0 = FMT == kNVINT4 ? 0.5f : 0.25f;
+  constexpr float kQ = FMT == kInt8 ? 127.0f : (FMT == kNVINT4 ? 7.0f : 6.0f);
+  constexpr float kD0 = (FMT == kNVINT4 || FMT == kInt8) ? 0.5f : 0.25f;
   float s_min = __fdiv_rn(__fsub_rn(amax, __fsqrt_rn(E0)), kQ);
   s_min = s_min < 0.0f ? 0.0f : s_min;
   uint32_t srt[BS];
@@ -528,9 +565,10 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
   for (int i = 0; i < BS; ++i) y = (i == kidx) ? __uint_as_float(srt[i]) : y;
   float s_max = __fdiv_rn(y, kD0);
   if (noise || !(s_min <= s_max)) return;
-  if (FMT == kTable) {
+  if (FMT == kTable || FMT == kInt8) {
     lo = table_count_below(s_min, false);
     hi = table_count_below(s_max, true) - 1;
+    if (FMT == kInt8 && lo < 1) lo = 1;  // index 0 (scale 0) is not a candidate
   } else if (FMT == kNVFP4 || FMT == kNVINT4) {
     lo = e4m3_ceil_code(s_min);
     hi = e4m3_floor_code(s_max);
@@ -734,10 +772,67 @@ __device__ __forceinline__ void write_block_int4(const QuantArgs& p, int64_t b, 
   }
 }
 
+// INT8 outputs of one block (int8/reference.py:36-62): quants =
+// clamp(round(x / s), -127, 127) by IEEE division with the reference's x86 NaN
+// payloads, dequant fl(q s) (the scale's NaN first).  packed: one int8 per
+// element (0x80 for a NaN quant); scale code: the E4M3 byte of 127 s (its
+// index in the candidate table); dq_bf16 rounded to nearest.
+template <int BS, int DT>
+__device__ __forceinline__ void write_block_int8(const QuantArgs& p, int64_t b, const float (&x)[BS], float s) {
+  const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
+#pragma unroll
+  for (int w = 0; w < BS / 8; ++w) {  // eight elements per step, 16-byte / 8-byte stores
+    float q8[8], d8[8];
+    uint32_t bytes[2] = {0u, 0u};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float xv = x[8 * w + k];
+      const uint32_t xb = __float_as_uint(xv);
+      float q;
+      if (is_nan_bits(xb & 0x7fffffffu)) q = __uint_as_float(xb | 0x00400000u);
+      else if (snan) q = s;
+      else if (s == 0.0f && xv == 0.0f) q = __uint_as_float(0xffc00000u);
+      else {
+        q = rintf(__fdiv_rn(xv, s));
+        q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+      }
+      const bool qn = is_nan_bits(__float_as_uint(q) & 0x7fffffffu);
+      q8[k] = q;
+      d8[k] = snan ? s : (qn ? q : __fmul_rn(q, s));
+      bytes[k / 4] |= (qn ? 0x80u : ((uint32_t)__float2int_rn(q) & 0xffu)) << (8 * (k % 4));
+    }
+    if (p.packed) reinterpret_cast<uint2*>(p.packed + b * BS)[w] = make_uint2(bytes[0], bytes[1]);
+    if (p.dq_bf16) {
+      uint32_t h[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        h[k] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(d8[2 * k])) |
+               ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(d8[2 * k + 1])) << 16);
+      reinterpret_cast<uint4*>(p.dq_bf16 + b * BS)[w] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    if (p.quants) {
+      float4* o = reinterpret_cast<float4*>(p.quants + b * BS + 8 * w);
+      o[0] = make_float4(q8[0], q8[1], q8[2], q8[3]);
+      o[1] = make_float4(q8[4], q8[5], q8[6], q8[7]);
+    }
+    if (p.dq) {
+      float4* o = reinterpret_cast<float4*>(p.dq + b * BS + 8 * w);
+      o[0] = make_float4(d8[0], d8[1], d8[2], d8[3]);
+      o[1] = make_float4(d8[4], d8[5], d8[6], d8[7]);
+    }
+  }
+  if (p.scales) p.scales[b] = s;
+  if (p.scale_codes) p.scale_codes[b] = snan ? (uint8_t)0x7f : (uint8_t)table_count_below(s, false);
+}
+
 template <int BS, int FMT, int METHOD, int DT>
 __device__ __forceinline__ void write_block(const QuantArgs& p, int64_t b, const float (&x)[BS], float s) {
   if constexpr (FMT == kNVINT4) {
     write_block_int4<BS, DT>(p, b, x, s);
+    return;
+  }
+  if constexpr (FMT == kInt8) {
+    write_block_int8<BS, DT>(p, b, x, s);
     return;
   }
   constexpr int MODE = Mode<FMT, DT>::v;
@@ -919,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
   extern __shared__ __align__(128) unsigned char smem_raw[];
   CandTable& ctab = s_ctab;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (METHOD == kSSE || FMT == kTable) {
+  if (METHOD == kSSE || FMT == kTable || FMT == kInt8) {
     fill_cand_table<FMT>(ctab, p.table, p.n_table);
     __syncthreads();
   }
@@ -1020,7 +1115,7 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
       // (its SSE is E0 bit for bit and E0's key wins ties); it usually is lo.
       constexpr int CPI = G::kCpi;
       if (hi >= lo) {
-        const int cn = FMT == kTable ? table_count_below(s, false) : (int)e4m3_code(s);
+        const int cn = (FMT == kTable || FMT == kInt8) ? table_count_below(s, false) : (int)e4m3_code(s);
         if (cn == lo) ++lo;
         else if (cn == hi) --hi;
       }
@@ -1389,6 +1484,23 @@ static cudaError_t launch_nvint4_bs(const QuantArgs& p, int dtype, int method, i
     if (dtype == kDtBF16) return launch_q<BS, kNVINT4, kSSE, kDtBF16>(p, sms, st);
     if (dtype == kDtF16) return launch_q<BS, kNVINT4, kSSE, kDtF16>(p, sms, st);
     return launch_q<BS, kNVINT4, kSSE, kDtF32>(p, sms, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// INT8 naive / SSE at block 32 on the per-thread-block kernel (larger blocks
+// and the Hessian variant run in qz_int.cu).
+cudaError_t launch_quantize_int8_bs32(const QuantArgs& p, int dtype, int method, int num_sms, cudaStream_t st) {
+  if (p.n_blocks == 0) return cudaSuccess;
+  if (method == kNaive) {
+    if (dtype == kDtBF16) return launch_q<32, kInt8, kNaive, kDtBF16>(p, num_sms, st);
+    if (dtype == kDtF16) return launch_q<32, kInt8, kNaive, kDtF16>(p, num_sms, st);
+    return launch_q<32, kInt8, kNaive, kDtF32>(p, num_sms, st);
+  }
+  if (method == kSSE) {
+    if (dtype == kDtBF16) return launch_q<32, kInt8, kSSE, kDtBF16>(p, num_sms, st);
+    if (dtype == kDtF16) return launch_q<32, kInt8, kSSE, kDtF16>(p, num_sms, st);
+    return launch_q<32, kInt8, kSSE, kDtF32>(p, num_sms, st);
   }
   return cudaErrorInvalidValue;
 }
