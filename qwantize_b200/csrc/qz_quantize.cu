@@ -227,7 +227,7 @@ __device__ __forceinline__ void fill_cand_table(CandTable& t, const float* table
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
       const float v = i == 0 ? 0.0f : (i <= 126 ? __fdiv_rn(e4m3_value(i), 127.0f) : 3.0e38f);
       t.val[i] = v;
-      t.cn[i] = make_uint2(0u, 0u);
+      t.cn[i] = make_uint2(__float_as_uint(__frcp_rn(v)), 0u);
     }
     if (threadIdx.x == 0) t.n = 127;
     return;
@@ -301,16 +301,26 @@ __device__ __forceinline__ float int4_sse(const float (&a)[BS], float s, float r
   return sum8<BS>(d2);
 }
 
-// INT8 block SSE on |x| = a (int8/reference.py:65-83): q = round(a / s) by IEEE
-// division (the scales E4M3 / 127 carry full fp32 mantissas), rounded half to
-// even by the 1.5 * 2^23 add / subtract, clamped to 127 (NaN propagates);
-// d = a - fl(q s) rounds twice, as in the reference.
+// INT8 block SSE on |x| = a (int8/reference.py:65-83): q = round(a / s) (the
+// scales E4M3 / 127 carry full fp32 mantissas: the IEEE quotient decides near
+// half integers), rounded half to even by the 1.5 * 2^23 add / subtract,
+// clamped to 127 (NaN propagates); d = a - fl(q s) rounds twice, as in the
+// reference.  rc = RN(1/s).
+// round(a / s) by IEEE division; out of line: the search calls it rarely
+__device__ __noinline__ float int8_round_div(float a, float s) {
+  return __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
+}
 template <int BS>
-__device__ __forceinline__ float int8_sse(const float (&a)[BS], float s) {
+__device__ __forceinline__ float int8_sse(const float (&a)[BS], float s, float rc) {
   float d2[BS];
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
-    float q = __fadd_rn(__fadd_rn(__fdiv_rn(a[i], s), 12582912.0f), -12582912.0f);
+    // a * RN(1/s) is within 2^-15.4 of fl(a / s) below 128, so its rounding
+    // agrees unless it lies within 2^-14 of a half integer: then the quotient
+    // decides (s = 0 gives inf / NaN either way; above 128 both clamp)
+    const float y = __fmul_rn(a[i], rc);
+    float q = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
+    if (fabsf(fabsf(__fsub_rn(y, q)) - 0.5f) <= 0x1p-14f) q = int8_round_div(a[i], s);
     q = q > 127.0f ? 127.0f : q;
     const float d = __fsub_rn(a[i], __fmul_rn(q, s));
     d2[i] = __fmul_rn(d, d);
@@ -322,7 +332,7 @@ __device__ __forceinline__ float int8_sse(const float (&a)[BS], float s) {
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
   if constexpr (FMT == kNVINT4) return int4_sse<BS, DT>(a, t.val[code], __uint_as_float(t.cn[code].x));
-  else if constexpr (FMT == kInt8) return int8_sse<BS>(a, t.val[code]);
+  else if constexpr (FMT == kInt8) return int8_sse<BS>(a, t.val[code], __uint_as_float(t.cn[code].x));
   else
   if constexpr (DT != kDtF32 && FMT == kNVFP4) {
     const uint2 e = t.cn[code];
@@ -337,7 +347,7 @@ __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable&
 // the input is 16-bit; s0 = 0 (NVFP4 blocks below 6 * 2^-10) takes the generic one.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
-  if constexpr (FMT == kInt8) return int8_sse<BS>(a, s);
+  if constexpr (FMT == kInt8) return int8_sse<BS>(a, s, __frcp_rn(s));
   if constexpr (FMT == kNVINT4) {
     const uint32_t sb = __float_as_uint(s);
     return int4_sse<BS, DT>(a, s, sb > 0u && sb < 0x7f800000u ? __frcp_rn(s) : 0.0f);
