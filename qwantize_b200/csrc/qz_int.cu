@@ -545,7 +545,7 @@ cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, 
     return launch_quantize_nvint4(p, dtype, bs, method, num_sms, st);  // qz_quantize.cu
   }
   if (fmt == kInt8) {
-    if (bs == 32 && method != kHessian) return launch_quantize_int8_bs32(p, dtype, method, num_sms, st);
+    if (bs == 32) return launch_quantize_int8_bs32(p, dtype, method, num_sms, st);  // qz_quantize.cu
     switch (bs) {
       case 32: return launch_int_d<32, kInt8>(p, dtype, method, num_sms, st);
       case 64: return launch_int_d<64, kInt8>(p, dtype, method, num_sms, st);

@@ -362,7 +362,7 @@ __device__ __forceinline__ float base_sse(const float (&a)[BS], float s) {
 // NVINT4, nvint4/reference.py:258).
 template <int BS, int FMT = kNVFP4>
 __device__ __forceinline__ float block_clip(const float (&a)[BS], float s) {
-  float t = __fmul_rn(FMT == kNVINT4 ? 7.0f : 6.0f, s), v[BS];
+  float t = __fmul_rn(FMT == kInt8 ? 127.0f : (FMT == kNVINT4 ? 7.0f : 6.0f), s), v[BS];
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
     float c = __fsub_rn(a[i], t);
@@ -445,7 +445,23 @@ __device__ __forceinline__ float block_hess_ilp(const float (&x)[BS], const floa
       const float dq = snan ? s : (is_nan_bits(__float_as_uint(q) & 0x7fffffffu) ? q : __fmul_rn(q, s));
       r[i] = __fsub_rn(x[i], dq);
     }
-  } else if (MODE != kDiv && s > 0.0f) {  // 16-bit input with an E4M3 / UE8M0 scale
+  } else if constexpr (FMT == kInt8) {  // r = x - fl(q s), q = clamp(round(x / s)) with the reference's NaNs
+    const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
+#pragma unroll
+    for (int i = 0; i < BS; ++i) {
+      const uint32_t xb = __float_as_uint(x[i]);
+      float q;
+      if (is_nan_bits(xb & 0x7fffffffu)) q = __uint_as_float(xb | 0x00400000u);
+      else if (snan) q = s;
+      else if (s == 0.0f && x[i] == 0.0f) q = __uint_as_float(0xffc00000u);
+      else {
+        q = rintf(__fdiv_rn(x[i], s));
+        q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+      }
+      const float dq = snan ? s : (is_nan_bits(__float_as_uint(q) & 0x7fffffffu) ? q : __fmul_rn(q, s));
+      r[i] = __fsub_rn(x[i], dq);
+    }
+} else if (MODE != kDiv && s > 0.0f) {  // 16-bit input with an E4M3 / UE8M0 scale
     const float c = __fmul_rn(__frcp_rn(s), kBiasDown);
 #pragma unroll
     for (int i = 0; i < BS; i += 2) {
@@ -593,7 +609,7 @@ __device__ __forceinline__ void search_range(const float (&x)[BS], const float (
 
 template <int FMT>
 __device__ __forceinline__ float cand_value(int c) {
-  if constexpr (FMT == kTable) return s_ctab.val[c];
+  if constexpr (FMT == kTable || FMT == kInt8) return s_ctab.val[c];
   return (FMT == kNVFP4 || FMT == kNVINT4) ? e4m3_value(c) : pow2f(c - 127);
 }
 
@@ -1197,7 +1213,7 @@ __global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
   const int64_t j = blockIdx.x;
   const float* Hg = p.h_blocks + j * (BS * BS);
   for (int i = threadIdx.x; i < BS * BS; i += blockDim.x) Ht[(i % BS) * BS + i / BS] = Hg[i];
-  if (FMT == kTable) fill_cand_table<FMT>(s_ctab, p.table, p.n_table);
+  if (FMT == kTable || FMT == kInt8) fill_cand_table<FMT>(s_ctab, p.table, p.n_table);
   __syncthreads();
   const int64_t M = p.n_blocks / p.n_col_blocks;
   for (int64_t m = (int64_t)blockIdx.y * blockDim.x + threadIdx.x; m < M;
@@ -1498,10 +1514,27 @@ static cudaError_t launch_nvint4_bs(const QuantArgs& p, int dtype, int method, i
   return cudaErrorInvalidValue;
 }
 
-// INT8 naive / SSE at block 32 on the per-thread-block kernel (larger blocks
-// and the Hessian variant run in qz_int.cu).
+// INT8 at block 32 on the per-thread-block kernels (larger blocks run in qz_int.cu).
+template <int DT>
+static cudaError_t launch_hessian_int8_bs32(const QuantArgs& p, int num_sms, cudaStream_t st) {
+  const int64_t M = p.n_blocks / p.n_col_blocks;
+  int64_t gy = (M + 127) / 128;
+  const int64_t want = (int64_t)num_sms * 16;
+  const int64_t per_j = (want + p.n_col_blocks - 1) / p.n_col_blocks;
+  gy = gy < per_j ? gy : per_j;
+  if (gy < 1) gy = 1;
+  if (gy > 65535) gy = 65535;
+  hessian_kernel<32, kInt8, DT><<<dim3((unsigned)p.n_col_blocks, (unsigned)gy), 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_quantize_int8_bs32(const QuantArgs& p, int dtype, int method, int num_sms, cudaStream_t st) {
   if (p.n_blocks == 0) return cudaSuccess;
+  if (method == kHessian) {
+    if (dtype == kDtBF16) return launch_hessian_int8_bs32<kDtBF16>(p, num_sms, st);
+    if (dtype == kDtF16) return launch_hessian_int8_bs32<kDtF16>(p, num_sms, st);
+    return launch_hessian_int8_bs32<kDtF32>(p, num_sms, st);
+  }
   if (method == kNaive) {
     if (dtype == kDtBF16) return launch_q<32, kInt8, kNaive, kDtBF16>(p, num_sms, st);
     if (dtype == kDtF16) return launch_q<32, kInt8, kNaive, kDtF16>(p, num_sms, st);
