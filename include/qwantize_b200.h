@@ -89,7 +89,8 @@ extern "C" {
  * complement nibbles, element 2i in the low nibble of byte i (NVINT4,
  * n_blocks*bs/2 bytes) or one int8 per element (INT8, n_blocks*bs bytes), with
  * 0x8 / 0x80 marking a NaN quant, and `dq_bf16` rounded to nearest (INT8
- * dequant values need not fit bf16).
+ * dequant values need not fit bf16).  Their quants / dq / dq_bf16 and packed
+ * outputs must be 16-byte aligned (NVINT4 at block 16: packed 8-byte aligned).
  */
 QZ_API int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, int format,
                 int method, const float* h_blocks, int64_t n_col_blocks, float* scales,
