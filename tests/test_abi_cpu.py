@@ -79,3 +79,27 @@ def test_division_free_rounding_is_exact_for_fp16_and_bf16():
             ref = torch.bucketize(a / s, B)
             alt = (a[:, None] > (B * s)[None, :]).sum(-1)
             assert torch.equal(ref, alt), float(s)
+
+
+def test_integer_formats_validation_and_tables():
+    """NVINT4 / INT8 argument checks come before any device call; the INT8
+    candidate table is the E4M3 values divided by 127 in fp32."""
+    import ctypes
+
+    from qwantize_b200 import _lib
+    L = _lib.load()
+    buf = ctypes.create_string_buffer(64)
+    x = ctypes.addressof(buf) + (16 - ctypes.addressof(buf) % 16) % 16  # 16-byte aligned host address
+    st = L.qz_quantize(x, 1, 4, 64, _lib.FMT_NVINT4, 0, None, 0, None, None, None, None, None, None, None)
+    assert st == _lib.QZ_ERR_INVALID and b"expected one of (16, 32)" in L.qz_last_error()
+    st = L.qz_quantize(x, 1, 4, 16, _lib.FMT_INT8, 0, None, 0, None, None, None, None, None, None, None)
+    assert st == _lib.QZ_ERR_INVALID and b"expected one of (32, 64, 128, 256)" in L.qz_last_error()
+    st = L.qz_quantize(x, 1, 4, 32, _lib.FMT_INT8, 4, None, 0, None, None, None, None, None, None, None)
+    assert st == _lib.QZ_ERR_INVALID and b"naive, SSE and Hessian" in L.qz_last_error()
+    st = L.qz_quantize(x, 1, 4, 32, _lib.FMT_INT8, 0, None, 0, None, x + 4, None, None, None, None, None)
+    assert st == _lib.QZ_ERR_INVALID and b"16-byte aligned" in L.qz_last_error()
+    st = L.qz_quantize(x, 1, 4, 32, _lib.FMT_NVINT4, 2, None, 0, None, None, None, None, None, None, None)
+    assert st == _lib.QZ_ERR_INVALID and b"X or H_blocks" in L.qz_last_error()
+    e4 = _lib.scale_table(_lib.FMT_NVINT4)
+    assert torch.equal(e4, _lib.scale_table(_lib.FMT_NVFP4))
+    assert torch.equal(_lib.scale_table(_lib.FMT_INT8), e4 / 127.0)
