@@ -1,35 +1,26 @@
-// qz_int.cu -- INT8 block quantization (int8/reference.py; blocks of 32 to 256):
-// the symmetric integer grid on the same search skeleton as NVFP4 (naive scale,
-// SSE bounds, bounded exhaustive search, Hessian variant).  NVINT4, whose
-// blocks of 16 / 32 fit one lane, runs on the per-thread-block kernels of
-// qz_quantize.cu; the code here keeps its NVINT4 arithmetic for reference
-// but launches INT8 only.
-//
-//   quants = clamp(round(x / s), -Q, Q)   (round half to even)
-//   NVINT4: Q = 7,   s = e4m3(max(amax / 7, 1e-12)),  bs 16 / 32, candidates: E4M3
-//   INT8:   Q = 127, s = e4m3(max(amax, 1e-12)) / 127, bs 32..256, candidates: E4M3 / 127
+// qz_int.cu -- INT8 block quantization for blocks of 64, 128 and 256
+// (int8/reference.py): q = clamp(round(x / s), -127, 127), round half to even,
+// s = e4m3(max(amax, 1e-12)) / 127, candidates E4M3 / 127, on the search
+// skeleton of NVFP4 (naive scale, SSE bounds, bounded exhaustive search,
+// Hessian variant).  NVINT4 and INT8 at block 32 fit one lane per block and run
+// on the per-thread-block kernels of qz_quantize.cu.
 //
 // Layout: eight lanes per block (a warp holds four consecutive blocks); lane
 // g of a group holds elements g, g+8, g+16, ...  With that layout torch's CPU
-// row-sum order (rows of 16: acc[k] = v[k] + v[k+8]; rows of >= 32: 32
-// accumulators at stride 32, combined as ((acc[m] + acc[m+8]) + acc[m+16]) +
-// acc[m+24]) is local to each lane, followed by one left fold over the eight
-// lanes.  The bounds need |x| sorted: a bitonic network in shared memory,
-// then the sequential fp64 prefix (torch.cumsum) with early exit (the prefix
-// sums are non-decreasing).  Candidates are visited in ascending order with a
-// strict '<' per block, so no atomics are needed; the loop runs warp-uniform
-// (shuffles need the whole warp), groups with fewer candidates mask theirs.
+// row-sum order for rows of >= 32 (32 accumulators at stride 32, combined as
+// ((acc[m] + acc[m+8]) + acc[m+16]) + acc[m+24], then a left fold) is local to
+// each lane, followed by one left fold over the eight lanes.  The bounds need
+// |x| sorted: a bitonic network in shared memory, then the sequential fp64
+// prefix (torch.cumsum) with early exit (the prefix sums are non-decreasing).
+// Candidates are visited in ascending order with a strict '<' per block, so no
+// atomics are needed; the loop runs warp-uniform (shuffles need the whole
+// warp), groups with fewer candidates mask theirs.
 //
-// Rounding: NVINT4 with 16-bit inputs uses q = rint(x * RN(1/s)).  For a
-// 16-bit x and an E4M3 s, x/s is either a half-integer exactly or at least
-// about 2^-10 away from one, far beyond the 2^-23 error of the product, so q
-// equals round(x / s) except at exact ties; the SSE is blind to ties (both
-// neighbours leave |d| = s/2), and the written codes and the Hessian residual
-// resolve them exactly: a tie is |x - q s| == s/2 (q s is exact), and an odd q
-// moves to the even neighbour.  INT8 scales carry a full fp32 mantissa, so
-// INT8 (and fp32 input) divide with IEEE division.  NaN payloads follow the
-// reference on x86: x / s returns x's NaN, else s's NaN, 0 / 0 the default
-// NaN 0xffc00000; dequant returns the scale's NaN first.
+// Rounding: INT8 scales carry full fp32 mantissas, so quotients are IEEE
+// divisions; the searches round them half to even with the 1.5 * 2^23 add /
+// subtract on the FMA pipe.  NaN payloads follow the reference on x86: x / s
+// returns x's NaN, else s's NaN, 0 / 0 the default NaN 0xffc00000; dequant
+// returns the scale's NaN first.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -86,14 +77,6 @@ __device__ __forceinline__ float group_sum(const float (&v)[BS / 8]) {
 template <int FMT, int DT>
 __device__ __forceinline__ float int_q_exact(float x, float s, float rc, bool fast) {
   constexpr float Q = IntQ<FMT>::v;
-  if (FMT == kNVINT4 && DT != kDtF32 && fast) {
-    float q = rintf(__fmul_rn(x, rc));
-    if (fabsf(q) <= 8.0f) {
-      const float e = __fmaf_rn(-q, s, x);  // exact: q * s has <= 7 significant bits
-      if (fabsf(e) == __fmul_rn(0.5f, s) && (__float2int_rz(q) & 1)) q = __fadd_rn(q, e > 0.0f ? 1.0f : -1.0f);
-    }
-    return fminf(fmaxf(q, -Q), Q);  // fmax/fmin keep -0.0
-  }
   const uint32_t xb = __float_as_uint(x), sb = __float_as_uint(s);
   if (is_nan_bits(xb & 0x7fffffffu)) return __uint_as_float(xb | 0x00400000u);
   if (is_nan_bits(sb & 0x7fffffffu)) return s;
@@ -113,71 +96,15 @@ __device__ __forceinline__ float int_dq(float q, float s) {
 template <int BS, int FMT, int DT>
 __device__ __forceinline__ float int_sse(const float (&x)[BS / 8], float s, float rc, bool fast) {
   float d2[BS / 8];
-  if (FMT == kNVINT4 && DT != kDtF32 && fast) {
 #pragma unroll
-    for (int j = 0; j < BS / 8; ++j) {  // on |x|: the SSE is blind to ties and to the sign
-      const float a = fabsf(x[j]);
-      const float q = fminf(rintf(__fmul_rn(a, rc)), 7.0f);
-      const float d = __fmaf_rn(-q, s, a);
-      d2[j] = __fmul_rn(d, d);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < BS / 8; ++j) {  // on |x| (the SSE is sign-symmetric); NaN propagates
-      const float a = fabsf(x[j]);
-      const float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
-      const float qc = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
-      const float d = __fsub_rn(a, __fmul_rn(qc, s));
-      d2[j] = __fmul_rn(d, d);
-    }
+  for (int j = 0; j < BS / 8; ++j) {  // on |x| (the SSE is sign-symmetric); NaN propagates
+    const float a = fabsf(x[j]);
+    const float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
+    const float qc = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
+    const float d = __fsub_rn(a, __fmul_rn(qc, s));
+    d2[j] = __fmul_rn(d, d);
   }
   return group_sum<BS>(d2);
-}
-
-// One element's squared error for |x| = a at a candidate scale s > 0 (finite).
-template <int FMT, int DT>
-__device__ __forceinline__ float int_d2(float a, float s, float rc) {
-  float d;
-  if constexpr (FMT == kNVINT4 && DT != kDtF32) {
-    const float q = fminf(rintf(__fmul_rn(a, rc)), 7.0f);
-    d = __fmaf_rn(-q, s, a);
-  } else {
-    // rint of a / s >= 0 on the FMA pipe: (y + 1.5*2^23) - 1.5*2^23 is round
-    // half to even below 2^22, and above it still clamps to Q
-    float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
-    q = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
-    d = __fsub_rn(a, __fmul_rn(q, s));
-  }
-  return __fmul_rn(d, d);
-}
-
-// A whole block's SSE evaluated by one lane, in torch's row-sum order (rows of
-// 16: acc[k] = v[k] + v[k+8]; longer rows: per residue m, four stride-32
-// accumulators combined in order), folded residue by residue.
-template <int BS, int FMT, int DT, class ROW>
-__device__ __forceinline__ float lane_row_sse(const ROW& ax, float s, float rc) {
-  float r = 0.0f;
-  if constexpr (BS == 16) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float a = __fadd_rn(int_d2<FMT, DT>(ax[k], s, rc), int_d2<FMT, DT>(ax[k + 8], s, rc));
-      r = k ? __fadd_rn(r, a) : a;
-    }
-  } else {
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      float A[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        A[t] = int_d2<FMT, DT>(ax[m + 8 * t], s, rc);
-#pragma unroll
-        for (int jj = 1; jj < BS / 32; ++jj) A[t] = __fadd_rn(A[t], int_d2<FMT, DT>(ax[m + 8 * t + 32 * jj], s, rc));
-      }
-      const float a = __fadd_rn(__fadd_rn(__fadd_rn(A[0], A[1]), A[2]), A[3]);
-      r = m ? __fadd_rn(r, a) : a;
-    }
-  }
-  return r;
 }
 
 // sum(clamp(|x| - Q s, 0)^2) (nvint4/reference.py:144, int8/reference.py:200).
@@ -332,11 +259,6 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
     if (is_nan_bits(m)) {
       s = __uint_as_float(kNvNanBits);
       code = 0x7f;
-    } else if (FMT == kNVINT4) {
-      float c = __fdiv_rn(amax, 7.0f);
-      c = c < 1e-12f ? 1e-12f : c;
-      s = e4m3_snap_nonneg(c);
-      code = (int)e4m3_code(s);
     } else {
       const float v = e4m3_snap_nonneg(amax < 1e-12f ? 1e-12f : amax);
       code = (int)e4m3_code(v);
@@ -395,34 +317,6 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
                                            : nullptr;
       float best_E = METHOD == kSSE ? E0 : int_hess<BS, FMT, DT>(x, s, rc, s_fin, Hj, wr);
       int best_c = -1;
-      if constexpr (METHOD == kSSE && BS <= 32) {
-        // candidate-parallel: lane g of the group takes candidates lo + 8r + g
-        // over the whole block; the group keeps the lowest (E, code), which is
-        // the first minimum of the ascending scan
-#pragma unroll
-        for (int j = 0; j < NE; ++j) wr[g + 8 * j] = fabsf(x[j]);
-        __syncwarp();
-        const int n_rounds = (int)__reduce_max_sync(0xffffffffu, (unsigned)((n + 7) >> 3));
-        float axr[BS];
-#pragma unroll
-        for (int i = 0; i < BS; ++i) axr[i] = wr[i];
-#pragma unroll 1
-        for (int r = 0; r < n_rounds; ++r) {
-          const int jc = 8 * r + g;
-          const bool act = jc < n;
-          int c = act ? lo + jc : 0;
-          float E = __int_as_float(0x7f800000);
-          if (act) E = lane_row_sse<BS, FMT, DT>(axr, s_itab[c], s_irc[c]);
-#pragma unroll
-          for (int o = 1; o < 8; o <<= 1) {
-            const float E2 = __shfl_xor_sync(0xffffffffu, E, o);
-            const int c2 = __shfl_xor_sync(0xffffffffu, c, o);
-            if (E2 < E || (E2 == E && c2 < c)) { E = E2; c = c2; }
-          }
-          if (E < best_E) { best_E = E; best_c = c; }
-        }
-        __syncwarp();  // wr is rewritten by the next block
-      } else {
 #pragma unroll 1
       for (int it = 0; it < n_max; ++it) {
         const bool act = it < n;
@@ -441,7 +335,6 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
         }
         if (act && E < best_E) { best_E = E; best_c = ci; }
       }
-      }
       if (best_c >= 0) {
         s = s_itab[best_c];
         rc = s_irc[best_c];
@@ -458,19 +351,12 @@ __global__ void __launch_bounds__(kIThreads) int_kernel(QuantArgs p) {
       const float d = int_dq(q, s);
       const int64_t e = b * BS + g + 8 * j;
       const bool qn = is_nan_bits(__float_as_uint(q) & 0x7fffffffu);
-      nib[j] = qn ? (FMT == kNVINT4 ? 0x8u : 0x80u) : ((uint32_t)__float2int_rn(q) & (FMT == kNVINT4 ? 0xfu : 0xffu));
+      nib[j] = qn ? 0x80u : ((uint32_t)__float2int_rn(q) & 0xffu);
       if (valid) {
         if (p.quants) p.quants[e] = q;
         if (p.dq) p.dq[e] = d;
         if (p.dq_bf16) p.dq_bf16[e] = __bfloat16_as_ushort(__float2bfloat16_rn(d));
-        if (FMT == kInt8 && p.packed) p.packed[e] = (uint8_t)nib[j];
-      }
-    }
-    if (FMT == kNVINT4 && p.packed) {  // element 2i: low nibble of byte i
-#pragma unroll
-      for (int j = 0; j < NE; ++j) {
-        const uint32_t other = __shfl_xor_sync(0xffffffffu, nib[j], 1);
-        if (valid && !(g & 1)) p.packed[(b * BS + g + 8 * j) >> 1] = (uint8_t)(nib[j] | (other << 4));
+        if (p.packed) p.packed[e] = (uint8_t)nib[j];
       }
     }
     if (valid && g == 0) {
@@ -547,7 +433,6 @@ cudaError_t launch_quantize_int(const QuantArgs& p, int dtype, int bs, int fmt, 
   if (fmt == kInt8) {
     if (bs == 32) return launch_quantize_int8_bs32(p, dtype, method, num_sms, st);  // qz_quantize.cu
     switch (bs) {
-      case 32: return launch_int_d<32, kInt8>(p, dtype, method, num_sms, st);
       case 64: return launch_int_d<64, kInt8>(p, dtype, method, num_sms, st);
       case 128: return launch_int_d<128, kInt8>(p, dtype, method, num_sms, st);
       case 256: return launch_int_d<256, kInt8>(p, dtype, method, num_sms, st);
