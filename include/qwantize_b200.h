@@ -205,6 +205,16 @@ QZ_API int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, const u
  */
 QZ_API int qz_poll_device_error(int clear, unsigned* flags_out);
 
+/*
+ * qz_selftest_wait -- exercises the bounded device-side wait that every kernel
+ * of this library uses: one warp waits on an mbarrier that nothing arrives
+ * on, gives up after limit_ns (at most 1e9), records bit 0 of the device error
+ * flags and returns.  Afterwards qz_poll_device_error reports QZ_ERR_TIMEOUT
+ * and the context stays usable.  For tests of the failure path; no
+ * counterpart in the reference, whose kernels have no device-side waits.
+ */
+QZ_API int qz_selftest_wait(uint64_t limit_ns, void* stream);
+
 /* Host helpers. */
 QZ_API int qz_scale_table(int format, float* out_host, int* n_out); /* 126 / 254 ascending values */
 QZ_API const char* qz_last_error(void);

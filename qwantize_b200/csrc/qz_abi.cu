@@ -70,6 +70,14 @@ int qz_poll_device_error(int clear, unsigned* flags_out) {
   return QZ_OK;
 }
 
+int qz_selftest_wait(uint64_t limit_ns, void* stream) {
+  if (limit_ns > 1000000000ull) return fail(QZ_ERR_INVALID, "limit_ns must be at most 1e9 (one second)");
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  return cuda_status(launch_wait_selftest(limit_ns, static_cast<cudaStream_t>(stream)), "qz_selftest_wait launch");
+}
+
 int qz_device_ok(void) {
   int sms = 0;
   return current_sms(&sms);
@@ -114,8 +122,6 @@ static int quantize_int(const void* x, int x_dtype, int64_t n_blocks, int block_
   if ((quants && !aligned(quants, 16)) || (dq && !aligned(dq, 16)) || (dq_bf16 && !aligned(dq_bf16, 16)) ||
       (packed && !aligned(packed, format == QZ_FMT_NVINT4 && block_size == 16 ? 8 : 16)))
     return fail(QZ_ERR_INVALID, "quants/dq/dq_bf16 must be 16-byte aligned, packed 8/16-byte aligned");
-  if ((quants && !aligned(quants, 4)) || (dq && !aligned(dq, 4)) || (dq_bf16 && !aligned(dq_bf16, 2)))
-    return fail(QZ_ERR_INVALID, "quants/dq must be 4-byte aligned, dq_bf16 2-byte aligned");
   if (method == QZ_METHOD_HESSIAN) {
     if (!h_blocks) return fail(QZ_ERR_INVALID, "X or H_blocks required");
     if (n_col_blocks <= 0 || n_blocks % n_col_blocks != 0 || n_col_blocks > 2147483647LL)

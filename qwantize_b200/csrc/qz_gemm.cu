@@ -222,7 +222,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = full + G::kStages;
   uint64_t* tfull = empty + G::kStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* mma_done = tempty + 2;  // the MMA issuer's final commit (all its MMAs retired)
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_base_s + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -230,6 +231,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 128); }
+    mbar_init(mma_done, 1);
     *abort_s = 0;
     fence_barrier_init();
   }
@@ -284,7 +286,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-    producer_done:;
+    producer_done:
+      // Before the CTA can exit, every load issued must have landed (after an
+      // abort the MMA issuer stops consuming): wait, bounded, on the phase of
+      // the last load issued into each stage.  In a normal run these phases
+      // have long completed and each wait returns at once.
+      for (uint32_t k = it > (uint32_t)G::kStages ? it - G::kStages : 0u; k < it; ++k)
+        mbar_wait_bounded(full + (k % G::kStages), (k / G::kStages) & 1, kDevErrLoadTimeout);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -322,6 +330,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!ok) break;
         umma_commit(tfull + acc);
       }
+      // the MMAs issued must retire before TMEM is freed (also after an abort)
+      umma_commit(mma_done);
+      mbar_wait_bounded(mma_done, 0u, kDevErrMmaTimeout);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
@@ -555,21 +566,12 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
 }
 
 
-// Token rows per full-Gram launch (QZ_GRAM_SEGMENT overrides; a multiple of 64).
-static int64_t gram_segment_rows() {
-  int64_t seg = 262144;
-  if (const char* v = getenv("QZ_GRAM_SEGMENT")) seg = atoll(v);
-  if (seg < 64) seg = 64;
-  return seg / 64 * 64;
-}
-
-// MN-major descriptor offsets; overridable for validation (QZ_MN_LBO / QZ_MN_SBO).
-static void mn_offsets(uint32_t* lbo, uint32_t* sbo) {
-  *lbo = 8192;  // between 64-element swizzle atoms along M / N
-  *sbo = 1024;  // between 8-row groups along K
-  if (const char* v = getenv("QZ_MN_LBO")) *lbo = (uint32_t)atoi(v);
-  if (const char* v = getenv("QZ_MN_SBO")) *sbo = (uint32_t)atoi(v);
-}
+// Full Gram: token rows per segment (a multiple of 64) and tile rows per band.
+constexpr int64_t kGramSegmentRows = 262144;
+constexpr int64_t kGramBand = 4;
+// MN-major descriptor offsets: 8 KB between 64-element swizzle atoms along M / N,
+// 1 KB between 8-row groups along K.
+constexpr uint32_t kMnLbo = 8192, kMnSbo = 1024;
 
 // ---------------------------------------------------------------------------
 // Fixed scratch for qz_gram_full_noalloc: the full Gram's per-tile segment
@@ -580,21 +582,39 @@ constexpr int64_t kNoAllocMaxTiles = 65536;
 static __device__ __align__(256) int g_noalloc_tile_counters[kNoAllocMaxTiles];
 
 // Device address of the array for the current device.  In host code the
-// array's name is only a stand-in, so the address is looked up once per device
-// (with that device current) and cached.
+// array's name is only a stand-in, so the address is looked up (with that
+// device current) and cached.  The cache is keyed on the current CUDA context
+// as well: after cudaDeviceReset the module is loaded again, possibly at
+// another address, and the next call looks the address up afresh.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
 static int noalloc_counters(int** out) {
   static std::mutex mu;
   static int* addr[64] = {nullptr};
+  static CUcontext ctx_of[64] = {nullptr};
+  static CtxGetCurrentFn get_ctx = nullptr;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(QZ_ERR_INVALID, "device index %d out of range", dev);
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  if (!get_ctx) {
+    void* fp = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fp, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(QZ_ERR_CUDA, "cuCtxGetCurrent unavailable");
+    get_ctx = reinterpret_cast<CtxGetCurrentFn>(fp);
+  }
+  CUcontext ctx = nullptr;  // NULL until the runtime has made a context current
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return fail(QZ_ERR_CUDA, "cuCtxGetCurrent failed");
+  if (!addr[dev] || !ctx || ctx_of[dev] != ctx) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_tile_counters);
+    e = cudaGetSymbolAddress(&p, g_noalloc_tile_counters);  // also makes the primary context current
     if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress (no-alloc scratch)");
+    if (get_ctx(&ctx) != CUDA_SUCCESS) return fail(QZ_ERR_CUDA, "cuCtxGetCurrent failed");
     addr[dev] = static_cast<int*>(p);
+    ctx_of[dev] = ctx;
   }
   *out = addr[dev];
   return QZ_OK;
@@ -631,7 +651,8 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   if (reinterpret_cast<uintptr_t>(X) % 16) return fail(QZ_ERR_INVALID, "X must be 16-byte aligned");
   GemmParams p{};
   p.K = K; p.M = 0; p.bs = block_size; p.H = H;
-  mn_offsets(&p.lbo, &p.sbo);
+  p.lbo = kMnLbo;
+  p.sbo = kMnSbo;
   p.tiles_m = (K + kBM - 1) / kBM;
   int sms = 0;
   int s = current_sms(&sms);
@@ -645,11 +666,10 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
     int64_t n = 0;
     for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
     p.tiles_per_seg = n;
-    p.seg_rows = gram_segment_rows();
+    p.seg_rows = kGramSegmentRows;
     const int64_t n_segs = (T + p.seg_rows - 1) / p.seg_rows;
     p.n_tiles = n * n_segs;
-    p.band = 4;
-    if (const char* v = getenv("QZ_GRAM_BAND")) p.band = atoll(v) > 0 ? atoll(v) : 4;
+    p.band = kGramBand;
     p.T = T;
     p.accumulate = accumulate;
     CUtensorMap map;
@@ -752,12 +772,12 @@ extern "C" int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int
   s = cuda_status(cudaMemsetAsync(counters, 0, (size_t)n * sizeof(int), st), "cudaMemsetAsync (counters)");
   if (s != QZ_OK) return s;
   p.K = K; p.M = 0; p.bs = 16; p.H = H; p.T = T; p.accumulate = accumulate;
-  mn_offsets(&p.lbo, &p.sbo);
+  p.lbo = kMnLbo;
+  p.sbo = kMnSbo;
   p.tiles_per_seg = n;
-  p.seg_rows = gram_segment_rows();
+  p.seg_rows = kGramSegmentRows;
   p.n_tiles = n * ((T + p.seg_rows - 1) / p.seg_rows);
-  p.band = 4;
-  if (const char* v = getenv("QZ_GRAM_BAND")) p.band = atoll(v) > 0 ? atoll(v) : 4;
+  p.band = kGramBand;
   p.seq = counters;
   CUtensorMap map;
   s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);

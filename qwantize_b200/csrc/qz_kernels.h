@@ -41,6 +41,8 @@ cudaError_t launch_unpack(const uint8_t* packed, int64_t n_bytes, int8_t* out, i
 cudaError_t launch_weight_sums(const void* W, int wdt, const void* Wdq, int ddt, int64_t n,
                                double* sums, int num_sms, cudaStream_t st);
 
+cudaError_t launch_wait_selftest(uint64_t limit_ns, cudaStream_t st);
+
 cudaError_t read_device_error_quantize(unsigned* out, bool clear);
 cudaError_t read_device_error_gemm(unsigned* out, bool clear);
 cudaError_t read_device_error_int(unsigned* out, bool clear);

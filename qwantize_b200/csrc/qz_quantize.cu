@@ -1080,7 +1080,15 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
   for (int64_t i = 0;; ++i) {
     const int64_t ch = gwarp + i * nwarps;
     if (ch >= n_chunks) break;
-    if (!mbar_wait_bounded(bar + (i % S), (uint32_t)((i / S) & 1), kDevErrLoadTimeout)) return;
+    const bool landed = mbar_wait_bounded(bar + (i % S), (uint32_t)((i / S) & 1), kDevErrLoadTimeout);
+    if (!__all_sync(0xffffffffu, landed)) {  // the whole warp leaves together
+      // a copy never landed: wait (bounded) for this warp's copies still in
+      // flight, that one included, so none lands after the CTA has exited
+      if (lane == 0)
+        for (int64_t k = i; k < i + S && gwarp + k * nwarps < n_chunks; ++k)
+          mbar_wait_bounded(bar + (k % S), (uint32_t)((k / S) & 1), kDevErrLoadTimeout);
+      return;
+    }
     const int64_t blk = ch * 32 + lane;
     const bool valid = blk < p.n_blocks;
     float x[BS];
@@ -1562,6 +1570,25 @@ cudaError_t launch_quantize(const QuantArgs& p, int dtype, int bs, int fmt, int 
                          : launch_fmt<16, kMXFP4>(p, dtype, method, num_sms, st);
   return fmt == kNVFP4 ? launch_fmt<32, kNVFP4>(p, dtype, method, num_sms, st)
                        : launch_fmt<32, kMXFP4>(p, dtype, method, num_sms, st);
+}
+
+// Self-test of the bounded wait: one warp waits on an mbarrier that nothing
+// ever arrives on.  The wait gives up after limit_ns, sets kDevErrLoadTimeout
+// in this unit's error flag and the kernel returns normally; no copy or
+// tensor-core operation is in flight, so the context stays usable.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  mbar_wait_bounded(&bar, 0u, kDevErrLoadTimeout, limit_ns);  // phase 0 never completes
+}
+
+cudaError_t launch_wait_selftest(uint64_t limit_ns, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns);
+  return cudaGetLastError();
 }
 
 cudaError_t read_device_error_quantize(unsigned* out, bool clear) {

@@ -22,7 +22,13 @@ Outputs (all small; large cases are stored as SHA-256 digests):
 
 ``--only int`` regenerates int_small.npz alone; ``--only int-digests`` writes
 int_digests.json (SHA-256 of the NVINT4 / INT8 outputs on the full config-0/1
-weight).
+weight); ``--only tail`` writes tail_small.npz (ragged block counts, every
+function); ``--only hessian-config2`` writes hessian_config2.npz: the reference's
+H-optimal scale choices (NVFP4 and the repaired MXFP4, blocks of 16 and 32) on
+the full 2560x9728 config weight, with the block Hessians they were given.
+
+The reference checkout is a required argument (the script never guesses a
+path).
 """
 from __future__ import annotations
 
@@ -177,6 +183,69 @@ def make_int_digests(q):
         json.dump(dg, f, indent=1, sort_keys=True)
 
 
+def scale_codes(s: torch.Tensor, fmt: int) -> np.ndarray:
+    """One byte per block: the E4M3 byte of an NVFP4 scale (0x7f for NaN) or
+    the UE8M0 biased exponent of an MXFP4 scale (0xff for NaN)."""
+    if fmt == 0:
+        return s.to(torch.float8_e4m3fn).view(torch.uint8).numpy().reshape(-1)
+    b = s.contiguous().view(torch.int32).numpy().reshape(-1).astype(np.int64)
+    e = (b >> 23) & 0xFF
+    return np.where(np.isnan(s.numpy().reshape(-1)), 0xFF, e).astype(np.uint8)
+
+
+def make_hessian_config2(q):
+    """H-optimal at the BASELINE config-2 weight (2560x9728, seed 0): the
+    reference's nvfp4_optimal_hessian (nvfp4/reference.py:266-407) and the
+    repaired mxfp4_optimal_hessian (mxfp4/reference.py:241-374) fed the same
+    block Hessians, built by the reference's own fp32 addmm loop from 32,768
+    seeded synthetic activation tokens.  Stores H and one scale byte per
+    block (hessian_config2.npz, about 4 MB)."""
+    M, K, T = 2560, 9728, 32768
+    Wf = make_weight(M, K, seed=0)
+    X = make_activations(T, K, seed=41, chunk_tokens=8192)
+    out = {"weight_sha256": hashlib.sha256(bits(Wf).tobytes()).hexdigest(),
+           "X_sha256": hashlib.sha256(bits(X).tobytes()).hexdigest(),
+           "M": M, "K": K, "T": T, "w_seed": 0, "x_seed": 41, "x_chunk": 8192, "torch": torch.__version__}
+    mx_hess = fixed_mxfp4_hessian(q)
+    for bs in (16, 32):
+        H = ref_block_hessians(X, bs)
+        out[f"H_{bs}"] = H.numpy()
+        Wb = Wf.reshape(M, K // bs, bs)
+        s, _ = q.nvfp4_optimal_hessian(Wb, H_blocks=H)
+        out[f"nv_{bs}_codes"] = scale_codes(s, 0)
+        assert np.array_equal(torch.from_numpy(out[f"nv_{bs}_codes"]).view(torch.float8_e4m3fn).float().numpy()
+                              .view(np.uint32), s.reshape(-1).numpy().view(np.uint32))
+        print("nvfp4 hessian", bs, flush=True)
+        s, _ = mx_hess(Wb, H_blocks=H)
+        out[f"mx_{bs}_codes"] = scale_codes(s, 1)
+        print("mxfp4 hessian", bs, flush=True)
+    np.savez_compressed(os.path.join(HERE, "hessian_config2.npz"), **out)
+
+
+def make_tail(q):
+    """Ragged block counts (tail_small.npz): a 37 x 544 weight is 1258 blocks of
+    16 or 629 blocks of 32, neither a multiple of the 32-block chunk a warp
+    owns, through every naive / optimal / *_torch function and the H-optimal
+    searches (block Hessians from seeded activations)."""
+    W = make_weight(37, 544, seed=51)
+    X = make_activations(3000, 544, seed=52, chunk_tokens=1024)
+    out = {"W": bits(W)}
+    mx_hess = fixed_mxfp4_hessian(q)
+    for bs in (16, 32):
+        Wb = W.reshape(37, 544 // bs, bs)
+        for name, _, _ in QUANT_FUNCS:
+            s, qq, dq = getattr(q, name)(Wb, return_dequant=True)
+            key = f"{name}_{bs}"
+            out[key + "_scales"], out[key + "_quants"], out[key + "_dq"] = s.numpy(), qq.numpy(), dq.numpy()
+        H = ref_block_hessians(X, bs)
+        out[f"H_{bs}"] = H.numpy()
+        s, qq, dq = q.nvfp4_optimal_hessian(Wb, return_dequant=True, H_blocks=H)
+        out[f"nv_H_{bs}_scales"], out[f"nv_H_{bs}_quants"] = s.numpy(), qq.numpy()
+        s, qq, dq = mx_hess(Wb, return_dequant=True, H_blocks=H)
+        out[f"mx_H_{bs}_scales"], out[f"mx_H_{bs}_quants"] = s.numpy(), qq.numpy()
+    np.savez_compressed(os.path.join(HERE, "tail_small.npz"), **out)
+
+
 def main(ref_root: str, skip_digests: bool = False, only: str = None):
     sys.path.insert(0, ref_root)
     import qwantize as q
@@ -186,6 +255,12 @@ def main(ref_root: str, skip_digests: bool = False, only: str = None):
     # ---- small quantization fixtures --------------------------------------
     W = make_weight(48, 1024, seed=11)
     E = edge_blocks().to(torch.bfloat16)
+    if only == "tail":
+        make_tail(q)
+        return
+    if only == "hessian-config2":
+        make_hessian_config2(q)
+        return
     if only == "int-digests":
         make_int_digests(q)
         return
@@ -318,5 +393,7 @@ def main(ref_root: str, skip_digests: bool = False, only: str = None):
 if __name__ == "__main__":
     args = [a for i, a in enumerate(sys.argv[1:], 1)
             if not a.startswith("--") and sys.argv[i - 1] != "--only"]
-    main(args[0] if args else "/root/reference", skip_digests="--skip-digests" in sys.argv,
+    if not args:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout> [--only NAME] [--skip-digests]")
+    main(args[0], skip_digests="--skip-digests" in sys.argv,
          only=sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None)

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests._golden import load, n_diff_bits, same_bits
+from tests._golden import hessian_parity, load, n_diff_bits, same_bits
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -46,11 +46,11 @@ def test_exotic_hoptimal(oracle, tname, bs):
     s, qq, dq = exotic.quantize_table(W.reshape(M, K // bs, bs), t, "hoptimal", return_dequant=True, H_blocks=H)
     os_, oq, odq = oracle.quantize_table(g["W"], bs, 2, g[f"table_{tname}"], H=H.numpy())
     assert same_bits(s.cpu().numpy(), os_) and same_bits(dq.cpu().numpy(), odq)
-    ref = g[f"{tname}_{bs}_hoptimal"].reshape(-1)
-    same = (dq.cpu().numpy().reshape(-1) == ref).mean()
-    assert same >= 0.999, same
+    ref = g[f"{tname}_{bs}_hoptimal"]
+    xf = W.float().cpu().numpy()
+    hessian_parity(xf, dq.cpu().numpy(), ref, H.numpy(), grid="dq")
     dq2 = exotic.fp4_hoptimal(W, X.to(DEV), t, bs)
-    assert (dq2.cpu().numpy().reshape(-1) == ref).mean() >= 0.999
+    hessian_parity(xf, dq2.cpu().numpy(), ref, H.numpy(), grid="dq")
 
 
 @pytest.mark.parametrize("bs", [16, 32])

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests._golden import load
+from tests._golden import hessian_parity, load
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -38,6 +38,21 @@ def test_gram_full(T, K):
     H = gram(X.to(DEV), "full")
     torch.cuda.synchronize()
     assert torch.equal(H, H.T), "H must be exactly symmetric"
+    _check_h(H, X)
+
+
+def test_gram_full_multi_segment():
+    """600,000 tokens is three 262,144-row segments of the full Gram: each
+    tile's segments are added in segment order through per-tile counters, so
+    H is deterministic (two calls agree bit for bit) and exactly symmetric."""
+    from qwantize_b200.hessian import gram
+    X = _x(600000, 256, 5)
+    Xg = X.to(DEV)
+    H = gram(Xg, "full")
+    H2 = gram(Xg, "full")
+    torch.cuda.synchronize()
+    assert torch.equal(H, H2)
+    assert torch.equal(H, H.T)
     _check_h(H, X)
 
 
@@ -70,7 +85,8 @@ def test_gram_empty_tokens_is_zero():
 
 def test_hessian_X_path_vs_reference():
     """nvfp4_optimal_hessian(W, X=X) / mxfp4 with the tensor-core Gram against
-    the reference's X path: >= 99.9% identical scales."""
+    the reference's X path: >= 99.9% identical scales, differing blocks within
+    1e-5 relative objective."""
     import qwantize_b200 as q
     from qwantize_b200.synthetic import make_activations
     g = load("hessian_small.npz")
@@ -84,14 +100,14 @@ def test_hessian_X_path_vs_reference():
         Href = torch.from_numpy(g[f"H_{bs}"])
         rel = ((Hb - Href).abs().max() / Href.abs().max()).item()
         assert rel < 1e-4, rel  # two fp32 summation orders of T = 4096 terms
+        xf = W.float().numpy()
         s, _ = q.nvfp4_optimal_hessian(Wb, X=X.to(DEV))
-        same = (s.cpu().numpy().reshape(-1) == g[f"nv_X_{bs}_scales"].reshape(-1)).mean()
-        assert same >= 0.999, same
+        # objectives of differing blocks measured with the reference's H
+        hessian_parity(xf, s.cpu().numpy(), g[f"nv_X_{bs}_scales"], g[f"H_{bs}"])
         s2, _ = q.nvfp4_optimal_hessian_triton(Wb, X=X.to(DEV))
         assert torch.equal(s, s2)
         s, _ = q.mxfp4_optimal_hessian(Wb, X=X.to(DEV))
-        same = (s.cpu().numpy().reshape(-1) == g[f"mx_X_{bs}_scales"].reshape(-1)).mean()
-        assert same >= 0.999, same
+        hessian_parity(xf, s.cpu().numpy(), g[f"mx_X_{bs}_scales"], g[f"H_{bs}"])
 
 
 def test_compute_metrics_vs_reference():

@@ -27,7 +27,10 @@ def test_noalloc_gram_matches_qz_gram_twice():
     L = _lib.load()
     dev = torch.device("cuda", 0)
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-    for T, K, seed in ((3000, 384, 1), (70000, 512, 2)):
+    # 600,000 tokens span three 262,144-row segments: a segment's add waits on
+    # the tile's counter, so stale counters from the previous call would let a
+    # later segment run before the first one's overwrite and drop its sum
+    for T, K, seed in ((3000, 384, 1), (70000, 512, 2), (600000, 256, 3)):
         X = _x(T, K, seed).to(dev)
         ref = torch.empty(K, K, device=dev)
         _lib.check(L.qz_gram(ctypes.c_void_p(X.data_ptr()), T, K, _lib.GRAM_FULL, 16, 0,
