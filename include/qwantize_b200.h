@@ -98,6 +98,34 @@ QZ_API int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_s
                 uint16_t* dq_bf16, void* stream);
 
 /*
+ * qz_quantize_grouped -- qz_quantize (NVFP4 / MXFP4, methods NAIVE and SSE)
+ * over many inputs in one persistent launch per 256 inputs.  Replaces the
+ * reference's row-chunked caller loops, which call one quantization function
+ * per matrix or row range (experiments/quant_bench.py:107-117,
+ * bench/full_bench.py:54-89): the chunks of 32 blocks of all inputs form one
+ * work list, so small inputs (one GPU's row shard of a k_proj, say) share the
+ * GPU instead of each launch filling a fraction of a wave.
+ *   items    host array of n_items descriptors (read during the call only);
+ *            each input and its outputs follow qz_quantize's rules (x and the
+ *            fp32 / bf16 outputs 16-byte aligned, packed 8 / 16-byte aligned,
+ *            NULL outputs skipped); all items share dtype, block size, format
+ *            and method.  Results are bit-identical to one qz_quantize per item.
+ */
+typedef struct QzQuantItem {
+  const void* x;
+  int64_t n_blocks;
+  float* scales;
+  float* quants;
+  float* dq;
+  uint8_t* scale_codes;
+  uint8_t* packed;
+  uint16_t* dq_bf16;
+} QzQuantItem;
+
+QZ_API int qz_quantize_grouped(const QzQuantItem* items, int n_items, int x_dtype, int block_size, int format,
+                               int method, void* stream);
+
+/*
  * qz_quantize_table -- qz_quantize with a caller-supplied scale grid: `table`
  * is a device array of n_table (2..256) ascending positive fp32 scales, e.g.
  * the unsigned 8-bit UE4M4 / UE5M3 grids of exotic_scales.py:17-57.  Follows

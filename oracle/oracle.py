@@ -73,11 +73,14 @@ def _dtype_code(x: np.ndarray, bf16: bool) -> int:
     return DT_F32
 
 
-def quantize(x, bs, fmt, method, H=None, bf16=True, want_dq=True, threads=None):
+def quantize(x, bs, fmt, method, H=None, bf16=True, want_dq=True, threads=None, counts=False):
     """Quantize a flat array of n_blocks*bs elements.
 
     x: uint16 bf16 bit patterns (bf16=True), float16 or float32.
-    Returns (scales, quants, dq, n_candidates_visited).
+    Returns (scales, quants, dq, n_candidates_in_range); with counts=True the
+    last item is (n_in_range, n_full_evaluations): candidates inside the
+    search bounds, and those that passed the clipping fast-fail and had their
+    full error evaluated (the reference's own loop, nvfp4/reference.py:191-228).
     """
     x = np.ascontiguousarray(x).reshape(-1)
     n_blocks = x.size // bs
@@ -112,7 +115,10 @@ def quantize(x, bs, fmt, method, H=None, bf16=True, want_dq=True, threads=None):
     else:
         with ThreadPoolExecutor(threads) as ex:
             ncand = sum(ex.map(run, ranges))
-    return scales, quants, dq, ncand
+    # the C side counts in-range candidates in the low 32 bits and full
+    # evaluations in the high bits of each range's total
+    n_in, n_full = ncand & 0xFFFFFFFF, ncand >> 32
+    return scales, quants, dq, ((n_in, n_full) if counts else n_in)
 
 
 def e4m3_snap(v: float) -> float:

@@ -5,6 +5,7 @@ the same function names, keyword arguments, (..., block_size) blocked layout
 and (scales, quants[, W_dq]) returns, computed by hand-written CUDA kernels
 behind the C ABI in include/qwantize_b200.h.  Naive and SSE results are
 bit-identical to the reference's pure-PyTorch path."""
+from .core import quantize_many
 from .fp4 import fp4_unpack
 from .int8 import int8_dequantize, int8_naive, int8_optimal, int8_optimal_hessian, int8_quantize_packed
 from .metrics import compute_metrics

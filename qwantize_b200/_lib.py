@@ -26,8 +26,15 @@ EXPORTS = [
     "qz_quantize", "qz_dequantize", "qz_dequantize_packed", "qz_fp4_unpack", "qz_gram",
     "qz_weight_error_sums", "qz_output_error_sums", "qz_scale_table", "qz_last_error",
     "qz_version", "qz_device_ok", "qz_poll_device_error", "qz_gram_full_noalloc", "qz_admm",
-    "qz_quantize_table", "qz_selftest_wait",
+    "qz_quantize_table", "qz_selftest_wait", "qz_quantize_grouped",
 ]
+
+
+class QzQuantItem(ctypes.Structure):
+    """One input of qz_quantize_grouped (include/qwantize_b200.h)."""
+    _fields_ = [("x", ctypes.c_void_p), ("n_blocks", ctypes.c_int64), ("scales", ctypes.c_void_p),
+                ("quants", ctypes.c_void_p), ("dq", ctypes.c_void_p), ("scale_codes", ctypes.c_void_p),
+                ("packed", ctypes.c_void_p), ("dq_bf16", ctypes.c_void_p)]
 
 _lib = None
 
@@ -59,6 +66,7 @@ def load():
     L.qz_scale_table.argtypes = [i32, vp, vp]
     L.qz_poll_device_error.argtypes = [i32, vp]
     L.qz_selftest_wait.argtypes = [ctypes.c_uint64, vp]
+    L.qz_quantize_grouped.argtypes = [vp, i32, i32, i32, i32, i32, vp]
     L.qz_last_error.restype = ctypes.c_char_p
     for name in EXPORTS:
         if name not in ("qz_last_error",):

@@ -143,3 +143,64 @@ def admm_fp32(W, dim, return_dequant, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.
     if return_dequant:
         res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev),)
     return res
+
+
+def quantize_many(weights, fmt, method, block_size=16, packed=True, return_dequant=False, outputs=None):
+    """Quantize a list of weights (fmt "nvfp4" / "mxfp4", method "naive" /
+    "optimal"; each (..., K) with K a multiple of
+    block_size, blocks along the last dimension, all of one dtype and device)
+    in one grouped launch per 256 weights (qz_quantize_grouped): the chunks
+    of every weight share the GPU, so many small matrices (row shards of a
+    layer stack) run as one wave-filling launch.  Results are bit-identical to
+    one call per weight.
+
+    packed=True returns, per weight, (scale_codes (..., K/bs) uint8, packed
+    (..., K/bs, bs/2) uint8[, dq bf16]); packed=False returns the reference's
+    fp32 (scales, quants[, dq]) shaped (..., K/bs[, bs]).  ``outputs`` may
+    supply preallocated tuples of the same layout (device tensors)."""
+    fmt = {"nvfp4": L.FMT_NVFP4, "mxfp4": L.FMT_MXFP4}.get(fmt, fmt)
+    method = {"naive": L.METHOD_NAIVE, "optimal": L.METHOD_SSE}.get(method, method)
+    assert block_size in (16, 32), f"block_size={block_size}, expected one of (16, 32)"
+    assert fmt in (L.FMT_NVFP4, L.FMT_MXFP4), "grouped launches run NVFP4 and MXFP4"
+    assert method in (L.METHOD_NAIVE, L.METHOD_SSE), "grouped launches run the naive and SSE methods"
+    if not weights:
+        return []
+    dev = cuda_device(weights[0])
+    dt = weights[0].dtype
+    items = (L.QzQuantItem * len(weights))()
+    keep, results = [], []
+    for i, W in enumerate(weights):
+        assert W.dtype == dt, "all weights of a grouped call share one dtype"
+        assert W.shape[-1] % block_size == 0, f"last dimension {W.shape[-1]} is not a multiple of {block_size}"
+        x = W.to(dev, non_blocking=True).contiguous().reshape(-1, block_size)
+        if x.data_ptr() % 16:
+            x = x.clone()
+        N = x.shape[0]
+        bshape = (*W.shape[:-1], W.shape[-1] // block_size)
+        if outputs is not None:
+            out = outputs[i]
+        elif packed:
+            out = (torch.empty(bshape, dtype=torch.uint8, device=dev),
+                   torch.empty(*bshape, block_size // 2, dtype=torch.uint8, device=dev))
+            if return_dequant:
+                out = out + (torch.empty(*bshape, block_size, dtype=torch.bfloat16, device=dev),)
+        else:
+            out = (torch.empty(bshape, dtype=torch.float32, device=dev),
+                   torch.empty(*bshape, block_size, dtype=torch.float32, device=dev))
+            if return_dequant:
+                out = out + (torch.empty(*bshape, block_size, dtype=torch.float32, device=dev),)
+        it = items[i]
+        it.x, it.n_blocks = x.data_ptr(), N
+        if packed:
+            it.scale_codes, it.packed = out[0].data_ptr(), out[1].data_ptr()
+            it.dq_bf16 = out[2].data_ptr() if len(out) > 2 else None
+        else:
+            it.scales, it.quants = out[0].data_ptr(), out[1].data_ptr()
+            it.dq = out[2].data_ptr() if len(out) > 2 else None
+        keep.append(x)
+        results.append(out)
+    L.check(L.load().qz_quantize_grouped(items, len(weights), L.dtype_code(x.dtype), block_size, fmt, method,
+                                         L.stream_ptr(dev)), "qz_quantize_grouped")
+    if weights[0].device != dev:
+        results = [tuple(t.to(weights[0].device) for t in r) for r in results]
+    return results

@@ -179,6 +179,56 @@ int qz_quantize(const void* x, int x_dtype, int64_t n_blocks, int block_size, in
                      "qz_quantize launch");
 }
 
+int qz_quantize_grouped(const QzQuantItem* items, int n_items, int x_dtype, int block_size, int format,
+                        int method, void* stream) {
+  if (block_size != 16 && block_size != 32)
+    return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", block_size);
+  if (format != QZ_FMT_NVFP4 && format != QZ_FMT_MXFP4)
+    return fail(QZ_ERR_INVALID, "qz_quantize_grouped supports NVFP4 and MXFP4, got format %d", format);
+  if (method != QZ_METHOD_NAIVE && method != QZ_METHOD_SSE)
+    return fail(QZ_ERR_INVALID, "qz_quantize_grouped supports the naive and SSE methods, got %d", method);
+  if (x_dtype != QZ_DTYPE_F32 && x_dtype != QZ_DTYPE_BF16 && x_dtype != QZ_DTYPE_F16)
+    return fail(QZ_ERR_INVALID, "unknown dtype %d", x_dtype);
+  if (n_items < 0) return fail(QZ_ERR_INVALID, "n_items must be >= 0");
+  if (n_items == 0) return QZ_OK;
+  if (!items) return fail(QZ_ERR_INVALID, "items is NULL");
+  for (int i = 0; i < n_items; ++i) {
+    const QzQuantItem& it = items[i];
+    if (it.n_blocks < 0) return fail(QZ_ERR_INVALID, "item %d: n_blocks must be >= 0", i);
+    if (it.n_blocks == 0) continue;
+    if (!it.x || !aligned(it.x, 16)) return fail(QZ_ERR_INVALID, "item %d: x must be non-NULL and 16-byte aligned", i);
+    if ((it.quants && !aligned(it.quants, 16)) || (it.dq && !aligned(it.dq, 16)) ||
+        (it.dq_bf16 && !aligned(it.dq_bf16, 16)) || (it.packed && !aligned(it.packed, block_size == 16 ? 8 : 16)))
+      return fail(QZ_ERR_INVALID, "item %d: quants/dq/dq_bf16 must be 16-byte aligned, packed 8/16-byte aligned", i);
+  }
+  int sms = 0;
+  int st = current_sms(&sms);
+  if (st != QZ_OK) return st;
+  // Launches of up to kMaxGroupItems inputs; the descriptors travel as the
+  // kernel's parameter.
+  static thread_local GroupArgs g;
+  for (int i0 = 0; i0 < n_items; i0 += kMaxGroupItems) {
+    const int n = n_items - i0 < kMaxGroupItems ? n_items - i0 : kMaxGroupItems;
+    int64_t chunks = 0;
+    int m = 0;
+    for (int i = i0; i < i0 + n; ++i) {
+      const QzQuantItem& it = items[i];
+      if (it.n_blocks == 0) continue;
+      g.item[m] = GroupItem{it.x, it.n_blocks, chunks, it.scales, it.quants, it.dq, it.scale_codes, it.packed,
+                            it.dq_bf16};
+      chunks += (it.n_blocks + 31) / 32;
+      ++m;
+    }
+    g.n_items = m;
+    g.n_chunks = chunks;
+    st = cuda_status(launch_quantize_grouped(g, x_dtype, block_size, format, method, sms,
+                                             static_cast<cudaStream_t>(stream)),
+                     "qz_quantize_grouped launch");
+    if (st != QZ_OK) return st;
+  }
+  return QZ_OK;
+}
+
 int qz_admm(const void* x, int x_dtype, int64_t n_blocks, int block_size, const float* h_blocks,
             const float* hn_blocks, const float* minv_blocks, int64_t n_col_blocks, int n_outer, int n_inner,
             float rho, float* scales, float* quants, float* dq, uint8_t* scale_codes, uint8_t* packed,

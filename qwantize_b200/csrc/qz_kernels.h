@@ -21,6 +21,33 @@ struct QuantArgs {
   int n_table;
 };
 
+// One input of a grouped launch (qz_quantize_grouped): its blocks, outputs
+// and the index of its first chunk of 32 blocks in the launch's chunk space.
+struct GroupItem {
+  const void* x;
+  int64_t n_blocks;
+  int64_t chunk0;
+  float* scales;
+  float* quants;
+  float* dq;
+  uint8_t* scale_codes;
+  uint8_t* packed;
+  uint16_t* dq_bf16;
+};
+
+// Inputs per grouped launch: the descriptors travel as a kernel parameter
+// (256 x 72 bytes, inside the 32 KB parameter space), so no device memory is
+// needed for them.
+constexpr int kMaxGroupItems = 256;
+
+struct GroupArgs {
+  int n_items;
+  int64_t n_chunks;
+  GroupItem item[kMaxGroupItems];
+};
+
+cudaError_t launch_quantize_grouped(const GroupArgs& g, int dtype, int bs, int fmt, int method, int num_sms,
+                                    cudaStream_t st);
 cudaError_t launch_quantize_nvint4(const QuantArgs& p, int dtype, int bs, int method, int num_sms,
                                    cudaStream_t st);
 cudaError_t launch_quantize_int8_bs32(const QuantArgs& p, int dtype, int method, int num_sms, cudaStream_t st);

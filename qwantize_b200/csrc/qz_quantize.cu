@@ -1031,9 +1031,59 @@ struct MinCtas {
   static constexpr int v = METHOD != kSSE ? 1 : (BS == 16 ? ((FMT == kNVFP4 || FMT == kNVINT4) ? 3 : 4) : 2);
 };
 
-// Naive / SSE / argmin methods.
-template <int BS, int FMT, int METHOD, int DT>
-__global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantize_kernel(QuantArgs p) {
+// Where a warp's chunks come from.  A chunk is 32 consecutive blocks of one
+// input; locate() maps a chunk index to its input bytes, its block count (32
+// except at the end of an input) and its first block, advancing `cur`, an
+// item cursor that only moves forward (a warp visits chunks in ascending
+// order); outputs() gives the output pointers of item `cur`.
+//   SingleSrc: one input (qz_quantize).
+//   GroupSrc:  many inputs in one launch (qz_quantize_grouped), chunks
+//              numbered item after item.
+struct SingleSrc {
+  const QuantArgs& p;
+  __device__ __forceinline__ int64_t n_chunks() const { return (p.n_blocks + 31) / 32; }
+  template <int CHUNK_BYTES>
+  __device__ __forceinline__ void locate(int64_t ch, int& cur, const char*& x, int& nb, int64_t& blk0) const {
+    (void)cur;
+    x = static_cast<const char*>(p.x) + ch * (int64_t)CHUNK_BYTES;
+    const int64_t left = p.n_blocks - ch * 32;
+    nb = left < 32 ? (int)left : 32;
+    blk0 = ch * 32;
+  }
+  __device__ __forceinline__ const QuantArgs& outputs(int) const { return p; }
+};
+
+struct GroupSrc {
+  const GroupArgs& g;
+  __device__ __forceinline__ int64_t n_chunks() const { return g.n_chunks; }
+  template <int CHUNK_BYTES>
+  __device__ __forceinline__ void locate(int64_t ch, int& cur, const char*& x, int& nb, int64_t& blk0) const {
+    while (cur + 1 < g.n_items && ch >= g.item[cur + 1].chunk0) ++cur;
+    const GroupItem& it = g.item[cur];
+    const int64_t local = ch - it.chunk0;
+    x = static_cast<const char*>(it.x) + local * (int64_t)CHUNK_BYTES;
+    const int64_t left = it.n_blocks - local * 32;
+    nb = left < 32 ? (int)left : 32;
+    blk0 = local * 32;
+  }
+  __device__ __forceinline__ QuantArgs outputs(int cur) const {
+    const GroupItem& it = g.item[cur];
+    QuantArgs q{};
+    q.x = it.x;
+    q.n_blocks = it.n_blocks;
+    q.scales = it.scales;
+    q.quants = it.quants;
+    q.dq = it.dq;
+    q.scale_codes = it.scale_codes;
+    q.packed = it.packed;
+    q.dq_bf16 = it.dq_bf16;
+    return q;
+  }
+};
+
+// Naive / SSE / argmin methods: the work of one CTA.
+template <int BS, int FMT, int METHOD, int DT, class Src>
+__device__ __forceinline__ void quantize_cta(const Src& src, const float* table, int n_table) {
   using G = WarpGeom<BS, FMT, DT, METHOD>;
   constexpr int MODE = Mode<FMT, DT>::v;
   constexpr int S = G::kStages;
@@ -1041,7 +1091,7 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
   CandTable& ctab = s_ctab;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (METHOD == kSSE || FMT == kTable || FMT == kInt8) {
-    fill_cand_table<FMT>(ctab, p.table, p.n_table);
+    fill_cand_table<FMT>(ctab, table, n_table);
     __syncthreads();
   }
   unsigned char* wbase = smem_raw + warp * G::kBytesAligned;
@@ -1054,20 +1104,22 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
   uint64_t* bar = reinterpret_cast<uint64_t*>(
       wbase + S * G::kChunkBytes + G::kRowBytes + (G::kCoop ? 32 * 8 + 64 * 4 : 0));
 
-  const int64_t n_chunks = (p.n_blocks + 31) / 32;
+  const int64_t n_chunks = src.n_chunks();
   const int64_t gwarp = (int64_t)blockIdx.x * kWarps + warp;
   const int64_t nwarps = (int64_t)gridDim.x * kWarps;
-  const char* src = static_cast<const char*>(p.x);
+  int issue_cur = 0, work_cur = 0;  // item cursors of the loads and of the work
 
   auto issue = [&](int64_t i) {  // lane 0 only
     int64_t ch = gwarp + i * nwarps;
     if (ch >= n_chunks) return;
-    int64_t nb = p.n_blocks - ch * 32;
-    nb = nb < 32 ? nb : 32;
+    const char* xs;
+    int nb;
+    int64_t blk0;
+    src.template locate<G::kChunkBytes>(ch, issue_cur, xs, nb, blk0);
     uint32_t bytes = (uint32_t)(nb * BS * Elem<DT>::kSize);
     uint64_t* b = bar + (i % S);
     mbar_arrive_expect_tx(b, bytes);
-    bulk_load(stage + (i % S) * G::kChunkBytes, src + ch * (int64_t)G::kChunkBytes, bytes, b);
+    bulk_load(stage + (i % S) * G::kChunkBytes, xs, bytes, b);
   };
 
   if (lane == 0) {
@@ -1089,8 +1141,13 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
           mbar_wait_bounded(bar + (k % S), (uint32_t)((k / S) & 1), kDevErrLoadTimeout);
       return;
     }
-    const int64_t blk = ch * 32 + lane;
-    const bool valid = blk < p.n_blocks;
+    const char* xs;
+    int nbc;
+    int64_t blk0;
+    src.template locate<G::kChunkBytes>(ch, work_cur, xs, nbc, blk0);
+    const auto& p = src.outputs(work_cur);
+    const int64_t blk = blk0 + lane;
+    const bool valid = lane < nbc;
     float x[BS];
     uint32_t amax16 = 0;  // 16-bit inputs: amax of the raw magnitudes, two per word
     if (valid) {
@@ -1209,6 +1266,18 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantiz
     }
     if (valid) write_block<BS, FMT, METHOD, DT>(p, blk, x, s);
   }
+}
+
+template <int BS, int FMT, int METHOD, int DT>
+__global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v) quantize_kernel(QuantArgs p) {
+  quantize_cta<BS, FMT, METHOD, DT>(SingleSrc{p}, p.table, p.n_table);
+}
+
+// Many inputs in one persistent launch (NVFP4 / MXFP4, naive and SSE).
+template <int BS, int FMT, int METHOD, int DT>
+__global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v)
+    quantize_grouped_kernel(const __grid_constant__ GroupArgs g) {
+  quantize_cta<BS, FMT, METHOD, DT>(GroupSrc{g}, nullptr, 0);
 }
 
 // Hessian method: CTA (j, row chunk); the CTA's H_j lives (transposed) in
@@ -1443,6 +1512,56 @@ static cudaError_t launch_q(const QuantArgs& p, int num_sms, cudaStream_t st) {
   unsigned grid = (unsigned)(want < cap ? want : cap);
   quantize_kernel<BS, FMT, METHOD, DT><<<grid, kThreads, smem, st>>>(p);
   return cudaGetLastError();
+}
+
+template <int BS, int FMT, int METHOD, int DT>
+static cudaError_t launch_g(const GroupArgs& g, int num_sms, cudaStream_t st) {
+  using G = WarpGeom<BS, FMT, DT, METHOD>;
+  const int smem = kWarps * G::kBytesAligned;
+  static int s_per_sm[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int per_sm = dev < 64 ? s_per_sm[dev] : 0;
+  if (per_sm == 0) {
+    e = cudaFuncSetAttribute(quantize_grouped_kernel<BS, FMT, METHOD, DT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_grouped_kernel<BS, FMT, METHOD, DT>,
+                                                      kThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    if (dev < 64) s_per_sm[dev] = per_sm;
+  }
+  const int64_t want = (g.n_chunks + kWarps - 1) / kWarps;
+  const int64_t cap = (int64_t)num_sms * per_sm;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  quantize_grouped_kernel<BS, FMT, METHOD, DT><<<grid, kThreads, smem, st>>>(g);
+  return cudaGetLastError();
+}
+
+template <int BS, int FMT, int DT>
+static cudaError_t launch_g_method(const GroupArgs& g, int method, int num_sms, cudaStream_t st) {
+  if (method == kNaive) return launch_g<BS, FMT, kNaive, DT>(g, num_sms, st);
+  if (method == kSSE) return launch_g<BS, FMT, kSSE, DT>(g, num_sms, st);
+  return cudaErrorInvalidValue;
+}
+
+template <int BS, int FMT>
+static cudaError_t launch_g_dtype(const GroupArgs& g, int dtype, int method, int num_sms, cudaStream_t st) {
+  if (dtype == kDtBF16) return launch_g_method<BS, FMT, kDtBF16>(g, method, num_sms, st);
+  if (dtype == kDtF16) return launch_g_method<BS, FMT, kDtF16>(g, method, num_sms, st);
+  return launch_g_method<BS, FMT, kDtF32>(g, method, num_sms, st);
+}
+
+cudaError_t launch_quantize_grouped(const GroupArgs& g, int dtype, int bs, int fmt, int method, int num_sms,
+                                    cudaStream_t st) {
+  if (g.n_chunks == 0) return cudaSuccess;
+  if (bs == 16)
+    return fmt == kNVFP4 ? launch_g_dtype<16, kNVFP4>(g, dtype, method, num_sms, st)
+                         : launch_g_dtype<16, kMXFP4>(g, dtype, method, num_sms, st);
+  return fmt == kNVFP4 ? launch_g_dtype<32, kNVFP4>(g, dtype, method, num_sms, st)
+                       : launch_g_dtype<32, kMXFP4>(g, dtype, method, num_sms, st);
 }
 
 template <int BS, int FMT, int DT>

@@ -111,6 +111,20 @@ def gram_sharded(X_local: torch.Tensor, mode: str = "full", block_size: int = 16
     return H
 
 
+def hessian_search_sharded(fn: Callable, W: torch.Tensor, X_local: torch.Tensor, group=None,
+                           return_dequant: bool = False, gram_fn: Optional[Callable] = None):
+    """H-optimal quantization across ranks: each rank builds the block
+    Hessians of its own tokens (block-diagonal Gram), one all-reduce (sum,
+    fp32) gives every rank the full H_j, then each rank searches only its
+    share of W's rows (no further collective).  ``fn`` is a drop-in Hessian
+    function (``nvfp4_optimal_hessian`` ...) taking ``H_blocks=``; W is
+    (M, K/bs, bs) with the block dimension last.  Returns ``(row_range,
+    result)`` as ``quantize_sharded`` does."""
+    bs = W.shape[-1]
+    H = gram_sharded(X_local, "blockdiag", bs, group=group, gram_fn=gram_fn)
+    return quantize_sharded(fn, W, dim=-1, return_dequant=return_dequant, group=group, H_blocks=H)
+
+
 def compute_metrics_sharded(W, W_dq, X_local=None, group=None, sums_fn: Optional[Callable] = None):
     """compute_metrics with the tokens of X sharded over ranks: the output-error
     sums of the local rows are all-reduced (double); the weight error is

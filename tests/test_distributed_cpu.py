@@ -13,8 +13,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from qwantize_b200.distributed import (compute_metrics_sharded, gram_sharded, quantize_sharded,
-                                       shard_range, token_chunks)
+from qwantize_b200.distributed import (compute_metrics_sharded, gram_sharded, hessian_search_sharded,
+                                       quantize_sharded, shard_range, token_chunks)
 
 
 def test_shard_range_covers_and_balances():
@@ -88,6 +88,21 @@ def _worker(rank, world, port, out_dir):
     Hb = gram_sharded(X[t0:t1], "blockdiag", 16, gram_fn=_oracle_gram)
     Hbr = _oracle_gram(X, "blockdiag", 16)
     res["gram_bd"] = bool(((Hb - Hbr).abs() <= 1e-6 * Hbr.abs().max()).all())
+
+    # H-optimal: token-sharded block Gram + all-reduce, then rows sharded
+    def hess_fn(W_, dim=-1, return_dequant=False, H_blocks=None):
+        from oracle import oracle
+        x = W_.contiguous()
+        s, q, dq, _ = oracle.quantize(x.view(torch.int16).numpy().view(np.uint16), x.shape[-1], 0, 2,
+                                      H=H_blocks.float().numpy())
+        r = (torch.from_numpy(s).reshape(x.shape[:-1]), torch.from_numpy(q).reshape(x.shape))
+        return r + (torch.from_numpy(dq).reshape(x.shape),) if return_dequant else r
+    Wh = W.reshape(37, 16, 16)
+    (h0, h1), part = hessian_search_sharded(hess_fn, Wh, X[t0:t1], gram_fn=_oracle_gram)
+    H_all = gram_sharded(X[t0:t1], "blockdiag", 16, gram_fn=_oracle_gram)
+    whole = hess_fn(Wh, H_blocks=H_all)
+    res["hopt_rows"] = (h0, h1) == shard_range(37, world, rank)
+    res["hopt"] = all(torch.equal(a, b[h0:h1]) for a, b in zip(part, whole))
 
     def sums_fn(W_, Wdq_, X_):
         from oracle import oracle
