@@ -35,7 +35,8 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
+        src = os.path.join(HERE, "qz_oracle.c")
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
             build()
         L = ctypes.CDLL(LIB_PATH)
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int

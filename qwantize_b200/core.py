@@ -54,12 +54,26 @@ def quantize_fp32(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(16,
         L.ptr(x), L.dtype_code(x.dtype), N, bs, fmt, method, L.ptr(H_blocks), J,
         L.ptr(scales), L.ptr(quants), L.ptr(dq), None, None, None, L.stream_ptr(dev))
     L.check(st, "qz_quantize")
-    out_dev = W.device
-    res = (scales.reshape(*batch_shape).to(out_dev),
-           quants.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev))
+    res = (scales.reshape(*batch_shape), quants.reshape(*batch_shape, bs).movedim(-1, dim))
     if return_dequant:
-        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev),)
-    return res
+        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim),)
+    return to_host_like(res, W.device, dev)
+
+
+def to_host_like(res, want, dev):
+    """Return device results on `want`: unchanged on the GPU; for a CPU caller
+    the copies go to page-locked host tensors (PyTorch's cached pinned
+    allocator, so repeated calls reuse them) at full PCIe speed, all issued
+    before one synchronisation of the stream."""
+    if want.type != "cpu":
+        return tuple(t.to(want) for t in res)
+    out = []
+    for t in res:
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t, non_blocking=True)
+        out.append(h)
+    torch.cuda.current_stream(dev).synchronize()
+    return tuple(out)
 
 
 def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(16, 32)):
@@ -85,7 +99,7 @@ def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(1
     res = (codes.reshape(*batch_shape), packed.reshape(*batch_shape, pw))
     if return_dequant:
         res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim),)
-    return res
+    return to_host_like(res, W.device, dev)
 
 
 def dequantize(scales, quants, dim=-1, valid=(16, 32)):
@@ -101,7 +115,7 @@ def dequantize(scales, quants, dim=-1, valid=(16, 32)):
     out = torch.empty_like(q)
     L.check(L.load().qz_dequantize(L.ptr(s), L.ptr(q), s.numel(), bs, L.ptr(out),
                                    L.stream_ptr(dev)), "qz_dequantize")
-    return out.reshape(*batch_shape, bs).movedim(-1, dim).to(quants.device)
+    return to_host_like((out.reshape(*batch_shape, bs).movedim(-1, dim),), quants.device, dev)[0]
 
 
 def dequantize_native(scale_codes, packed, fmt, dtype=torch.bfloat16):
@@ -118,7 +132,7 @@ def dequantize_native(scale_codes, packed, fmt, dtype=torch.bfloat16):
     assert f32 is not None or b16 is not None, "dtype must be float32 or bfloat16"
     L.check(L.load().qz_dequantize_packed(L.ptr(p), L.ptr(c), n_blocks, bs, fmt, L.ptr(f32),
                                           L.ptr(b16), L.stream_ptr(dev)), "qz_dequantize_packed")
-    return out.to(packed.device)
+    return to_host_like((out,), packed.device, dev)[0]
 
 
 def admm_fp32(W, dim, return_dequant, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.0):
@@ -137,12 +151,26 @@ def admm_fp32(W, dim, return_dequant, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.
                           int(n_outer), int(n_inner), float(rho), L.ptr(scales), L.ptr(quants), L.ptr(dq),
                           None, None, None, L.stream_ptr(dev))
     L.check(st, "qz_admm")
-    out_dev = W.device
-    res = (scales.reshape(*batch_shape).to(out_dev),
-           quants.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev))
+    res = (scales.reshape(*batch_shape), quants.reshape(*batch_shape, bs).movedim(-1, dim))
     if return_dequant:
-        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim).to(out_dev),)
-    return res
+        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim),)
+    return to_host_like(res, W.device, dev)
+
+
+def to_host_like(res, want, dev):
+    """Return device results on `want`: unchanged on the GPU; for a CPU caller
+    the copies go to page-locked host tensors (PyTorch's cached pinned
+    allocator, so repeated calls reuse them) at full PCIe speed, all issued
+    before one synchronisation of the stream."""
+    if want.type != "cpu":
+        return tuple(t.to(want) for t in res)
+    out = []
+    for t in res:
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t, non_blocking=True)
+        out.append(h)
+    torch.cuda.current_stream(dev).synchronize()
+    return tuple(out)
 
 
 def quantize_many(weights, fmt, method, block_size=16, packed=True, return_dequant=False, outputs=None):

@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib as L
-from .core import _blocks, cuda_device
+from .core import _blocks, cuda_device, to_host_like
 
 _METHOD = {"naive": L.METHOD_NAIVE, "optimal": L.METHOD_SSE, "hoptimal": L.METHOD_HESSIAN}
 
@@ -69,11 +69,10 @@ def quantize_table(W, table, method="optimal", dim=-1, return_dequant=False, X=N
     L.check(L.load().qz_quantize_table(L.ptr(x), L.dtype_code(x.dtype), N, bs, meth, L.ptr(t), t.numel(),
                                        L.ptr(H), J, L.ptr(scales), L.ptr(quants), L.ptr(dq), None, None, None,
                                        L.stream_ptr(dev)), "qz_quantize_table")
-    res = (scales.reshape(*batch_shape).to(W.device),
-           quants.reshape(*batch_shape, bs).movedim(-1, dim_).to(W.device))
+    res = (scales.reshape(*batch_shape), quants.reshape(*batch_shape, bs).movedim(-1, dim_))
     if return_dequant:
-        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim_).to(W.device),)
-    return res
+        res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim_),)
+    return to_host_like(res, W.device, dev)
 
 
 # The experiment's entry points (experiments/quant_exotic_scales.py:48-182):
