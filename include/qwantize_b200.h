@@ -209,6 +209,27 @@ QZ_API int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int acc
                                 void* stream);
 
 /*
+ * qz_gptq -- GPTQ error compensation over all column blocks (replaces the
+ * loop of gptq_strided, experiments/quant_gptq_strided.py:49-135; the damped
+ * inverse Hessian Hi of :72-85 is the caller's input).  Column groups of
+ * group_cols (32, 64 or 128) columns run left to right: one kernel carries
+ * every row through the group's blocks (scale search by `method` as in
+ * qz_quantize on fp32 input, error d / Hi_cc, in-group update), then a
+ * tcgen05 GEMM subtracts E @ Hi[group, later columns] from the later columns,
+ * at fp32 accuracy (tf32 high / low operand pairs, three products).
+ *   Wb        (K/bs, M, bs) fp32 working weight, column-block-major, updated
+ *   Qb        (K/bs, M, bs) fp32 dequantized result
+ *   Hi        (K, K) fp32 damped inverse Hessian; Hi_split 2*K*K fp32 scratch
+ *   h_blocks  (K/bs, bs, bs) block Hessians for QZ_METHOD_HESSIAN, else NULL
+ *   E         M * 2 * group_cols fp32 scratch
+ *   loss      ceil(K / group_cols) * ceil(M / 64) doubles: sum of d^2 / Hi_cc
+ *             per (group, 64-row slice); the reference's loss is their sum / M
+ */
+QZ_API int qz_gptq(float* Wb, float* Qb, const float* Hi, float* Hi_split, const float* h_blocks, int64_t M,
+                   int64_t K, int block_size, int format, int method, int group_cols, float* E, double* loss,
+                   void* stream);
+
+/*
  * qz_weight_error_sums -- sums[0] += sum (W_dq - W)^2, sums[1] += sum W^2 in
  * double (metrics.py:23-27).  W and W_dq are n elements of w_dtype / dq_dtype.
  */

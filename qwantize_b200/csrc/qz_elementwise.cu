@@ -184,4 +184,34 @@ cudaError_t launch_weight_sums(const void* W, int wdt, const void* Wdq, int ddt,
   return cudaGetLastError();
 }
 
+// x = hi + lo with hi = tf32(x) (round to nearest, ties away) and lo = tf32(x -
+// hi): the operand split of the three-product tf32 GEMM (hi*hi + hi*lo +
+// lo*hi) that keeps GPTQ's error update at fp32 accuracy on the tensor cores.
+__global__ void split_tf32_kernel(const float4* __restrict__ src, float4* __restrict__ hi, float4* __restrict__ lo,
+                                  int64_t n4) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = src[i];
+    float in[4] = {v.x, v.y, v.z, v.w}, h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t r;
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(in[k]));
+      h[k] = __uint_as_float(r);
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(__fsub_rn(in[k], h[k])));
+      l[k] = __uint_as_float(r);
+    }
+    hi[i] = make_float4(h[0], h[1], h[2], h[3]);
+    lo[i] = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+cudaError_t launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, int num_sms, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  split_tf32_kernel<<<(unsigned)(num_sms * 8), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                            reinterpret_cast<float4*>(hi),
+                                                            reinterpret_cast<float4*>(lo), n / 4);
+  return cudaGetLastError();
+}
+
 }  // namespace qz

@@ -42,19 +42,21 @@ int current_sms(int* sms);
 constexpr int kGemmThreads = 192;
 constexpr int kBM = 128, kBK = 64;  // tile rows, K-step (64 bf16 = one 128-byte swizzle row)
 
-enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2 };
+enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3 };
 
 // Per-mode geometry.  Full Gram / metrics: 128 x 256 tiles, A 16 KB + B 32 KB
 // per stage, 4 stages, two 256-column accumulators (all 512 TMEM columns).
 // Block-diagonal Gram: 128 x 128 diagonal tiles whose A and B panels are the
 // same columns of X, so one 16 KB panel per stage feeds both operands; 8 stages.
+// GPTQ update: 128 x 128 tiles of fp32 operands as tf32 high / low pairs; a
+// stage holds 32 columns of K (128 bytes per row) of A_hi, A_lo, B_hi, B_lo.
 template <int MODE>
 struct Geo {
-  static constexpr int BN = MODE == kGramDiag ? 128 : 256;
-  static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = MODE == kGramDiag ? 0 : BN * kBK * 2;
+  static constexpr int BN = (MODE == kGramDiag || MODE == kGptq) ? 128 : 256;
+  static constexpr int kABytes = MODE == kGptq ? 2 * kBM * 128 : kBM * kBK * 2;
+  static constexpr int kBBytes = MODE == kGramDiag ? 0 : (MODE == kGptq ? 2 * BN * 128 : BN * kBK * 2);
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = MODE == kGramDiag ? 8 : 4;
+  static constexpr int kStages = MODE == kGramDiag ? 8 : (MODE == kGptq ? 3 : 4);
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -72,6 +74,10 @@ struct GemmParams {
   float* partials;      // kGramDiag: splits-1 partial (K/bs, bs, bs) buffers
   double* sums;
   uint32_t lbo, sbo;    // MN-major descriptor offsets (bytes)
+  // kGptq: W -= E @ Hi[group rows, columns c1..K) written into the
+  // column-block-major working weight Wb (nblk, M, bs)
+  float* Wb;
+  int64_t g0c, c1, gk;  // group's first column, first column after the group, group width
 };
 
 // ---------------------------------------------------------------------------
@@ -104,6 +110,17 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32 (fp32 containers, tf32
+// products, fp32 accumulate).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -147,6 +164,11 @@ __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool a_mn_major,
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::tf32: tf32 x tf32 -> fp32, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // ---------------------------------------------------------------------------
 // tile enumeration
 // ---------------------------------------------------------------------------
@@ -156,7 +178,7 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64
     nj = t / p.tiles_m;     // the split index
     return;
   }
-  if (mode == kMetrics) {
+  if (mode == kMetrics || mode == kGptq) {
     mi = t / p.tiles_n;
     nj = t % p.tiles_n;
     return;
@@ -193,6 +215,11 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t t) {
   if (MODE == kMetrics) {
     tile_coords(p, MODE, t, u.mi, u.nj);
     u.steps = (p.K + kBK - 1) / kBK;
+    return u;
+  }
+  if (MODE == kGptq) {
+    tile_coords(p, MODE, t, u.mi, u.nj);
+    u.steps = p.gk / 32;  // 32 fp32 columns (128 bytes) per stage
     return u;
   }
   if (MODE == kGramDiag) {
@@ -268,7 +295,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           unsigned char* sa = smem + s * G::kStageBytes;
           unsigned char* sb = sa + G::kABytes;
           mbar_arrive_expect_tx(full + s, G::kStageBytes);
-          if (MODE == kMetrics) {
+          if (MODE == kGptq) {
+            // A: the scaled errors (high parts, then low parts, of one row of E);
+            // B: rows c1 + n of Hi (high parts; the low parts are rows K + c1 + n),
+            // columns of the group (Hi is symmetric: B^T = Hi[c1 + n][group])
+            const int kx = (int)(ks * 32), ay = (int)(mi * kBM), by = (int)(p.c1 + nj * 128);
+            tma_load_2d(sa, &map_a, kx, ay, full + s);
+            tma_load_2d(sa + 16384, &map_a, (int)p.gk + kx, ay, full + s);
+            tma_load_2d(sb, &map_b, (int)p.g0c + kx, by, full + s);
+            tma_load_2d(sb + 16384, &map_b, (int)p.g0c + kx, (int)p.K + by, full + s);
+          } else if (MODE == kMetrics) {
             const int kx = (int)(ks * kBK);
             tma_load_2d(sa, &map_a, kx, (int)(mi * kBM), full + s);                 // X rows (t)
             tma_load_2d(sb, &map_b, kx, (int)(nj * 128), full + s);                 // W rows
@@ -297,8 +333,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr bool mn = MODE != kMetrics;
-      constexpr uint32_t idesc = instr_desc(kBM, BN, mn, mn);
+      constexpr bool mn = MODE != kMetrics && MODE != kGptq;
+      constexpr uint32_t idesc = MODE == kGptq ? instr_desc_tf32(kBM, BN) : instr_desc(kBM, BN, mn, mn);
       uint32_t it = 0, lt = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
         const int64_t k_steps = unit_of<MODE>(p, t).steps;
@@ -313,6 +349,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * G::kStageBytes);
           const uint32_t sb = MODE == kGramDiag ? sa : sa + G::kABytes;
+          if (MODE == kGptq) {
+            // D += A_hi B_hi + A_hi B_lo + A_lo B_hi, 8 tf32 (32 bytes) of K per MMA
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ah = smem_desc(sa + kk * 32, 16, 1024), al = smem_desc(sa + 16384 + kk * 32, 16, 1024);
+              const uint64_t bh = smem_desc(sb + kk * 32, 16, 1024), bl = smem_desc(sb + 16384 + kk * 32, 16, 1024);
+              umma_tf32(d_tmem, al, bh, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+              umma_tf32(d_tmem, ah, bl, idesc, 1u);
+              umma_tf32(d_tmem, ah, bh, idesc, 1u);
+            }
+            umma_commit(empty + s);
+            continue;
+          }
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             uint64_t ad, bd;
@@ -363,6 +412,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (trow < p.T) { part0 += (double)e; part1 += (double)r2; }
+      } else if (MODE == kGptq) {
+        // W[m, c] -= D for the tile's columns c = c1 + 128 nj + ..., written
+        // into the column-block-major working weight (16 consecutive columns
+        // of one row are 64 contiguous bytes of one block row)
+        const int64_t m = mi * kBM + row;
+        const int bs = p.bs;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          const int64_t col = p.c1 + nj * BN + c;
+          if (m >= p.M || col >= p.K) continue;
+          float4* d4 = reinterpret_cast<float4*>(p.Wb + ((col / bs) * p.M + m) * bs + col % bs);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float4 w = d4[q];
+            w.x -= v[4 * q]; w.y -= v[4 * q + 1]; w.z -= v[4 * q + 2]; w.w -= v[4 * q + 3];
+            d4[q] = w;
+          }
+        }
       } else if (MODE == kGramDiag && p.bs > 32) {
         // bs 64 / 128: the rows of this warp belong to one block, whose bs
         // columns start at cb inside the 128-wide tile (loads are warp-wide)
@@ -537,14 +606,14 @@ static EncodeTiledFn encode_fn() {
 
 // 2-D bf16 tensor map: rows of `inner` elements, `outer` rows, box inner x outer.
 static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                    uint32_t box_outer) {
+                    uint32_t box_outer, bool f32 = false) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(QZ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 2};
+  cuuint64_t strides[1] = {inner * (f32 ? 4 : 2)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QZ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -783,4 +852,56 @@ extern "C" int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int
   s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
   if (s != QZ_OK) return s;
   return launch_gemm<kGramFull>(map, map, map, p, st);
+}
+
+extern "C" int qz_gptq(float* Wb, float* Qb, const float* Hi, float* Hi_split, const float* h_blocks, int64_t M,
+                       int64_t K, int block_size, int format, int method, int group_cols, float* E, double* loss,
+                       void* stream) {
+  const int bs = block_size;
+  if (bs != 16 && bs != 32) return fail(QZ_ERR_INVALID, "block_size must be 16 or 32, got %d", bs);
+  if (format != QZ_FMT_NVFP4 && format != QZ_FMT_MXFP4) return fail(QZ_ERR_INVALID, "unknown format %d", format);
+  if (method != QZ_METHOD_NAIVE && method != QZ_METHOD_SSE && method != QZ_METHOD_HESSIAN)
+    return fail(QZ_ERR_INVALID, "qz_gptq supports the naive, SSE and Hessian methods, got %d", method);
+  if (group_cols != 32 && group_cols != 64 && group_cols != 128)
+    return fail(QZ_ERR_INVALID, "group_cols must be 32, 64 or 128, got %d", group_cols);
+  if (group_cols % bs) return fail(QZ_ERR_INVALID, "group_cols must be a multiple of block_size");
+  if (M < 0 || K <= 0 || K % bs) return fail(QZ_ERR_INVALID, "need M >= 0 and K a positive multiple of block_size");
+  if (K > 1073741823LL || M > 2147483647LL) return fail(QZ_ERR_INVALID, "M and K too large");
+  if (M == 0) return QZ_OK;
+  if (!Wb || !Qb || !Hi || !Hi_split || !E || !loss) return fail(QZ_ERR_INVALID, "NULL pointer");
+  if (method == QZ_METHOD_HESSIAN && !h_blocks) return fail(QZ_ERR_INVALID, "h_blocks required");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(Wb) | reinterpret_cast<uintptr_t>(Qb) |
+                       reinterpret_cast<uintptr_t>(Hi) | reinterpret_cast<uintptr_t>(Hi_split) |
+                       reinterpret_cast<uintptr_t>(E) | reinterpret_cast<uintptr_t>(h_blocks);
+  if (al % 16) return fail(QZ_ERR_INVALID, "all buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int sms = 0;
+  int s = current_sms(&sms);
+  if (s != QZ_OK) return s;
+  s = cuda_status(launch_split_tf32(Hi, Hi_split, Hi_split + K * K, K * K, sms, st), "split_tf32 launch");
+  if (s != QZ_OK) return s;
+  CUtensorMap map_e, map_h;
+  s = make_map(&map_e, E, (uint64_t)(2 * group_cols), (uint64_t)M, 32, 128, true);
+  if (s == QZ_OK) s = make_map(&map_h, Hi_split, (uint64_t)K, (uint64_t)(2 * K), 32, 128, true);
+  if (s != QZ_OK) return s;
+  const int64_t nblk = K / bs, gb = group_cols / bs;
+  const int64_t ctas = (M + kGptqRows - 1) / kGptqRows;
+  int64_t gi = 0;
+  for (int64_t g0 = 0; g0 < nblk; g0 += gb, ++gi) {
+    const int64_t gbn = nblk - g0 < gb ? nblk - g0 : gb;
+    const bool last = g0 + gbn >= nblk;
+    GptqGroupArgs a{Wb, Qb, Hi, h_blocks, last ? nullptr : E, loss + gi * ctas, M, K, (int)g0, (int)gbn,
+                    group_cols};
+    s = cuda_status(launch_gptq_group(a, bs, format == QZ_FMT_NVFP4 ? 0 : 1, method, st), "gptq group launch");
+    if (s != QZ_OK || last) break;
+    GemmParams p{};
+    p.M = M; p.K = K; p.bs = bs; p.Wb = Wb;
+    p.g0c = g0 * bs; p.c1 = (g0 + gbn) * bs; p.gk = group_cols;
+    p.tiles_m = (M + kBM - 1) / kBM;
+    p.tiles_n = (K - p.c1 + 127) / 128;
+    p.n_tiles = p.tiles_m * p.tiles_n;
+    s = launch_gemm<kGptq>(map_e, map_h, map_h, p, st);
+    if (s != QZ_OK) break;
+  }
+  return s;
 }

@@ -46,6 +46,26 @@ struct GroupArgs {
   GroupItem item[kMaxGroupItems];
 };
 
+// One column group of GPTQ (qz_gptq): quantize its column blocks left to
+// right for every row, propagating each block's scaled error into the rest of
+// the group; write the dequantized blocks, the scaled errors for the update
+// of the later columns, and per-CTA loss partials.
+struct GptqGroupArgs {
+  float* Wb;              // (nblk, M, bs) working weight, column-block-major
+  float* Qb;              // (nblk, M, bs) dequantized result
+  const float* Hi;        // (K, K) damped inverse Hessian
+  const float* h_blocks;  // (nblk, bs, bs) block Hessians (Hessian method) or NULL
+  float* E;               // (M, 2 * gk): tf32 high parts of the scaled errors, then the low parts; or NULL
+  double* loss;           // one partial per CTA
+  int64_t M, K;
+  int g0, gb, gk;         // first column block, blocks in this group, group width in columns (E stride)
+};
+
+constexpr int kGptqRows = 64;  // rows (threads) per CTA of the group kernel
+
+cudaError_t launch_gptq_group(const GptqGroupArgs& a, int bs, int fmt, int method, cudaStream_t st);
+cudaError_t launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, int num_sms, cudaStream_t st);
+
 cudaError_t launch_quantize_grouped(const GroupArgs& g, int dtype, int bs, int fmt, int method, int num_sms,
                                     cudaStream_t st);
 cudaError_t launch_quantize_nvint4(const QuantArgs& p, int dtype, int bs, int method, int num_sms,

@@ -1483,6 +1483,180 @@ cudaError_t launch_admm(const QuantArgs& qa, const float* h, const float* hn, co
 }
 
 // ---------------------------------------------------------------------------
+// GPTQ column group (experiments/quant_gptq_strided.py:49-135, gptq_strided):
+// one thread per row of W.  Rows are independent in GPTQ -- a row's later
+// columns depend only on its own earlier errors and the shared inverse
+// Hessian -- so a CTA of kGptqRows threads carries its rows through the whole
+// group: the group's columns live in shared memory (column-major, one word
+// per thread: conflict-free), with Hi's group block beside them (read as
+// broadcasts).  For every column block, left to right:
+//   choose the scale (naive / SSE / Hessian search: the same device code and
+//   arithmetic as qz_quantize on fp32 input), dequantize, d = w - q,
+//   err = d / Hi_cc, loss += d^2 / Hi_cc, and
+//   W[:, later columns of the group] -= err @ Hi[block rows, those columns].
+// The scaled errors leave as a tf32 high / low pair per element for the
+// tensor-core update of the columns after the group (qz_gemm.cu).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Scale of one fp32 block, exactly as quantize_kernel (naive, SSE) and
+// hessian_kernel (Hessian; Ht = H_j transposed in shared memory) choose it.
+template <int BS, int FMT, int METHOD>
+__device__ __forceinline__ float choose_scale_f32(const float (&x)[BS], const float* Ht) {
+  constexpr int MODE = Mode<FMT, kDtF32>::v;
+  float a[BS];
+  const uint32_t amax_bits = abs_and_amax<BS>(x, a);
+  float s = naive_scale<FMT>(amax_bits);
+  if (METHOD == kNaive || is_nan_bits(__float_as_uint(s) & 0x7fffffffu)) return s;
+  const float E0 = base_sse<BS, MODE, kDtF32, FMT>(a, s);
+  int lo, hi;
+  if constexpr (METHOD == kSSE) {
+    search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
+    float best = E0;
+#pragma unroll 1
+    for (int c = lo; c <= hi; ++c) {
+      const float E = cand_sse<BS, MODE, kDtF32, FMT>(a, s_ctab, c);
+      if (E < best) { best = E; s = s_ctab.val[c]; }
+    }
+  } else {
+    float best = block_hess_ilp<BS, MODE, kDtF32, FMT>(x, a, s, Ht);
+    search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
+#pragma unroll 1
+    for (int c = lo; c <= hi; ++c) {
+      const float sc = cand_value<FMT>(c);
+      const float Hc = block_clip<BS, FMT>(a, sc);
+      const bool pass = FMT != kMXFP4 ? (Hc < __fmul_rn(best, 10.0f)) : (Hc < E0);
+      if (!pass) continue;
+      const float E = block_hess_ilp<BS, MODE, kDtF32, FMT>(x, a, sc, Ht);
+      if (E < best) { best = E; s = sc; }
+    }
+  }
+  return s;
+}
+
+template <int BS, int FMT, int METHOD>
+__global__ void __launch_bounds__(kGptqRows) gptq_group_kernel(GptqGroupArgs A) {
+  constexpr int MODE = Mode<FMT, kDtF32>::v;
+  constexpr int R = kGptqRows;
+  extern __shared__ __align__(16) float gsm[];
+  const int gc = A.gb * BS;       // columns of this group
+  const int64_t c0 = (int64_t)A.g0 * BS;
+  float* Hg = gsm;                // gc x gc: Hi[c0 + r][c0 + c]
+  float* Wt = Hg + gc * gc;       // gc x R: column c of this CTA's rows
+  float* hd = Wt + gc * R;        // gc: Hi diagonal
+  float* Ht = hd + gc;            // BS x BS: H_j transposed (Hessian method)
+  __shared__ double red[R / 32];
+  const int t = threadIdx.x;
+  if (METHOD != kNaive) fill_cand_table<FMT>(s_ctab);
+  for (int i = t; i < gc * gc; i += R) Hg[i] = A.Hi[(c0 + i / gc) * A.K + c0 + i % gc];
+  for (int i = t; i < gc; i += R) hd[i] = A.Hi[(c0 + i) * A.K + c0 + i];
+  const int64_t m = (int64_t)blockIdx.x * R + t;
+  const bool valid = m < A.M;
+  for (int jj = 0; jj < A.gb; ++jj) {
+    const float4* src = reinterpret_cast<const float4*>(A.Wb + (((int64_t)A.g0 + jj) * A.M + m) * BS);
+#pragma unroll
+    for (int v = 0; v < BS / 4; ++v) {
+      const float4 w = valid ? src[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int c = jj * BS + 4 * v;
+      Wt[(c + 0) * R + t] = w.x;
+      Wt[(c + 1) * R + t] = w.y;
+      Wt[(c + 2) * R + t] = w.z;
+      Wt[(c + 3) * R + t] = w.w;
+    }
+  }
+  __syncthreads();
+  double loss = 0.0;
+  for (int jj = 0; jj < A.gb; ++jj) {
+    if (METHOD == kHessian) {
+      const float* Hj = A.h_blocks + ((int64_t)A.g0 + jj) * BS * BS;
+      for (int i = t; i < BS * BS; i += R) Ht[(i % BS) * BS + i / BS] = Hj[i];
+      __syncthreads();
+    }
+    float x[BS];
+#pragma unroll
+    for (int i = 0; i < BS; ++i) x[i] = Wt[(jj * BS + i) * R + t];
+    const float s = choose_scale_f32<BS, FMT, METHOD>(x, Ht);
+    const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
+    float err[BS], dq[BS];
+#pragma unroll
+    for (int i = 0; i < BS; ++i) {
+      // fp4_quantize * s (the generic path of write_block for fp32 input)
+      const float q = cb_rt((uint32_t)fp4_index<MODE>(fabsf(x[i]), s));
+      const float qs = x[i] > 0.0f ? q : (x[i] < 0.0f ? -q : 0.0f);
+      dq[i] = snan ? s : __fmul_rn(qs, s);
+      const float d = __fsub_rn(x[i], dq[i]);
+      const float h = hd[jj * BS + i];
+      err[i] = __fdiv_rn(d, h);
+      loss += (double)__fdiv_rn(__fmul_rn(d, d), h);
+    }
+    if (valid) {
+      float4* dst = reinterpret_cast<float4*>(A.Qb + (((int64_t)A.g0 + jj) * A.M + m) * BS);
+#pragma unroll
+      for (int v = 0; v < BS / 4; ++v) dst[v] = make_float4(dq[4 * v], dq[4 * v + 1], dq[4 * v + 2], dq[4 * v + 3]);
+      if (A.E) {
+        float* e = A.E + m * 2 * A.gk + jj * BS;
+#pragma unroll
+        for (int i = 0; i < BS; ++i) {
+          const float hi = tf32_rna(err[i]);
+          e[i] = hi;
+          e[A.gk + i] = tf32_rna(__fsub_rn(err[i], hi));
+        }
+      }
+    }
+    // the rest of the group: W[:, c] -= sum_i err_i * Hi[block row i][c]
+#pragma unroll 1
+    for (int c = (jj + 1) * BS; c < gc; ++c) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int i = 0; i < BS; ++i) acc = __fmaf_rn(err[i], Hg[(jj * BS + i) * gc + c], acc);
+      Wt[c * R + t] = __fsub_rn(Wt[c * R + t], acc);
+    }
+    if (METHOD == kHessian) __syncthreads();  // Ht is rewritten for the next block
+  }
+  if (!valid) loss = 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) loss += __shfl_xor_sync(0xffffffffu, loss, o);
+  if ((t & 31) == 0) red[t >> 5] = loss;
+  __syncthreads();
+  if (t == 0) {
+    double sum = 0.0;
+    for (int w = 0; w < R / 32; ++w) sum += red[w];
+    A.loss[blockIdx.x] = sum;
+  }
+}
+
+template <int BS, int FMT, int METHOD>
+static cudaError_t launch_gptq_t(const GptqGroupArgs& a, cudaStream_t st) {
+  const int gc = a.gb * BS;
+  const size_t smem = ((size_t)gc * gc + (size_t)gc * kGptqRows + gc + BS * BS) * 4;
+  cudaError_t e = cudaFuncSetAttribute(gptq_group_kernel<BS, FMT, METHOD>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = (unsigned)((a.M + kGptqRows - 1) / kGptqRows);
+  gptq_group_kernel<BS, FMT, METHOD><<<grid, kGptqRows, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int BS, int FMT>
+static cudaError_t launch_gptq_m(const GptqGroupArgs& a, int method, cudaStream_t st) {
+  if (method == kNaive) return launch_gptq_t<BS, FMT, kNaive>(a, st);
+  if (method == kSSE) return launch_gptq_t<BS, FMT, kSSE>(a, st);
+  if (method == kHessian) return launch_gptq_t<BS, FMT, kHessian>(a, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gptq_group(const GptqGroupArgs& a, int bs, int fmt, int method, cudaStream_t st) {
+  if (a.M == 0 || a.gb == 0) return cudaSuccess;
+  if (bs == 16)
+    return fmt == kNVFP4 ? launch_gptq_m<16, kNVFP4>(a, method, st) : launch_gptq_m<16, kMXFP4>(a, method, st);
+  return fmt == kNVFP4 ? launch_gptq_m<32, kNVFP4>(a, method, st) : launch_gptq_m<32, kMXFP4>(a, method, st);
+}
+
+// ---------------------------------------------------------------------------
 // host-side launch
 // ---------------------------------------------------------------------------
 template <int BS, int FMT, int METHOD, int DT>

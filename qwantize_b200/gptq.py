@@ -6,14 +6,15 @@ Follows experiments/quant_gptq_strided.py:49-135 (``gptq_strided``) and
 the inverse through its Cholesky factor, then quantize column blocks left to
 right, each block's scaled error propagated to all later columns.
 
-B200 layout: the working weight is kept column-block-major, (K/bs, M, bs), so
-every column block is one contiguous input of the quantization kernel (naive,
-SSE-optimal or Hessian-optimal, fp32 path: the same arithmetic as the
-reference's torch quantizers).  Error propagation is lazy-batched: inside a
-group of ``group`` columns the update touches only the group, and one batched
-GEMM per group applies the accumulated error to every later column (the
-standard GPTQ reordering of the same sums; results agree with the reference to
-floating-point reassociation).
+B200 layout: the working weight is kept column-block-major, (K/bs, M, bs).
+Rows are independent in GPTQ, so one kernel per group of ``group`` columns
+carries every row through the group's blocks in shared memory (scale search --
+naive, SSE-optimal or Hessian-optimal with the same arithmetic as the fp32
+quantization kernels -- error, in-group update), and one tcgen05 GEMM per
+group applies the group's scaled errors to every later column at fp32
+accuracy (tf32 high / low operand pairs).  This is the standard lazy-batch
+reordering of GPTQ's sums; results agree with the reference to floating-point
+reassociation.
 """
 from __future__ import annotations
 
@@ -58,7 +59,10 @@ def gptq(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "op
 
     W (M, K), H (K, K) -> (Q (M, K) fp32 dequantized, average per-row loss).
     ``H_blocks`` (K/bs, bs, bs) are the Hessians the H-optimal quantizer uses
-    for each column block (default: the diagonal blocks of H)."""
+    for each column block (default: the diagonal blocks of H).  ``group`` is
+    the width in columns (32, 64 or 128) of the column groups one kernel
+    carries through; the columns after a group are updated by one tensor-core
+    GEMM per group (qz_gptq)."""
     bs = block_size
     assert bs in (16, 32)
     dev = cuda_device(W)
@@ -66,40 +70,24 @@ def gptq(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "op
     M, K = W.shape
     assert K % bs == 0 and H.shape == (K, K)
     nblk = K // bs
+    group = max(bs, min(128, group))
+    assert group in (32, 64, 128) and group % bs == 0, "group must be 32, 64 or 128 columns"
     fmt_c, meth_c = _FMT[fmt], _METHOD[method]
     Hd = H.to(dev, torch.float32)
     Hi = _inverse_hessian(Hd, damp)
     if meth_c == L.METHOD_HESSIAN and H_blocks is None:
-        H_blocks = torch.stack([Hd[j * bs:(j + 1) * bs, j * bs:(j + 1) * bs] for j in range(nblk)])
+        H_blocks = Hd.reshape(nblk, bs, nblk, bs).diagonal(dim1=0, dim2=2).permute(2, 0, 1)
     if H_blocks is not None:
         H_blocks = H_blocks.to(dev, torch.float32).contiguous()
     # column-block-major working copy: Wb[j] is W[:, j*bs:(j+1)*bs]
     Wb = W.float().reshape(M, nblk, bs).permute(1, 0, 2).contiguous()
     Qb = torch.empty_like(Wb)
-    gb = max(1, group // bs)  # column blocks per lazy-batch group
-    # few host-issued launches per column block: the loop is bound by issue rate
-    h_diag_all = Hi.diagonal().contiguous().reshape(nblk, bs)
-    parts = torch.empty(nblk, dtype=torch.float64, device=dev)  # per-block loss, summed once
-    d = torch.empty(M, bs, dtype=torch.float32, device=dev)
-    for g0 in range(0, nblk, gb):
-        g1 = min(nblk, g0 + gb)
-        Eg = torch.empty(g1 - g0, M, bs, dtype=torch.float32, device=dev)  # scaled errors of the group
-        for j in range(g0, g1):
-            w_blk = Wb[j]
-            q = _quant_block(w_blk, bs, fmt_c, meth_c, H_blocks[j] if H_blocks is not None else None, Qb[j])
-            cs = j * bs
-            torch.sub(w_blk, q, out=d)
-            err = torch.div(d, h_diag_all[j], out=Eg[j - g0])
-            torch.sum(d * err, dim=(0, 1), dtype=torch.float64, out=parts[j])  # d^2 / h_jj
-            if j + 1 < g1:  # update the rest of the group: W[:, ce:g_end] -= err @ Hi[cs:ce, ce:g_end]
-                rest = g1 - j - 1
-                upd = torch.mm(err, Hi[cs:cs + bs, (j + 1) * bs:g1 * bs])  # (M, rest * bs)
-                Wb[j + 1:g1] -= upd.view(M, rest, bs).transpose(0, 1)
-        if g1 < nblk:  # everything after the group at once
-            rows = Hi[g0 * bs:g1 * bs, g1 * bs:]  # (group cols, rest)
-            E2 = Eg.permute(1, 0, 2).reshape(M, (g1 - g0) * bs)
-            upd = E2 @ rows  # (M, rest)
-            Wb[g1:] -= upd.reshape(M, nblk - g1, bs).permute(1, 0, 2)
+    Hs = torch.empty(2, K, K, dtype=torch.float32, device=dev)
+    E = torch.empty(M, 2 * group, dtype=torch.float32, device=dev)
+    n_groups = (K + group - 1) // group
+    parts = torch.zeros(n_groups * ((M + 63) // 64), dtype=torch.float64, device=dev)
+    L.check(L.load().qz_gptq(L.ptr(Wb), L.ptr(Qb), L.ptr(Hi), L.ptr(Hs), L.ptr(H_blocks), M, K, bs, fmt_c,
+                             meth_c, group, L.ptr(E), L.ptr(parts), L.stream_ptr(dev)), "qz_gptq")
     Q = Qb.permute(1, 0, 2).reshape(M, K)
     return Q, float(parts.sum().item()) / M
 

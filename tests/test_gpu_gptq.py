@@ -23,13 +23,16 @@ def _inputs():
     return W, H
 
 
+@pytest.mark.parametrize("group", [32, 64, 128])
 @pytest.mark.parametrize("bs", [16, 32])
 @pytest.mark.parametrize("method", ["naive", "optimal", "hoptimal"])
-def test_gptq_vs_reference(method, bs):
+def test_gptq_vs_reference(method, bs, group):
+    """Column groups of 32, 64 and 128 (the in-group update in the group
+    kernel, the rest on the tensor-core tf32x3 GEMM) all reach the bar."""
     from qwantize_b200.gptq import gptq
     W, H = _inputs()
     gg = load("gptq_small.npz")
-    Q, loss = gptq(W.to(DEV), H.to(DEV), "nvfp4", method, bs)
+    Q, loss = gptq(W.to(DEV), H.to(DEV), "nvfp4", method, bs, group=group)
     Qr = gg[f"{method}_{bs}_Q"]
     ref_loss = float(gg[f"{method}_{bs}_loss"][0])
     same = (Q.cpu().numpy() == Qr).mean()
@@ -52,3 +55,37 @@ def test_gptq_ordered_runs_and_beats_naive_quantization():
         E = Qm.float() - Wd.float()
         return float((E @ Hd * E).sum())
     assert out_err(Q) < out_err(dq.reshape(W.shape))
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4"])
+def test_gptq_ragged_rows_vs_strided_loop(fmt):
+    """200 rows (not a multiple of the 64-row CTA or the 128-row GEMM tile), K =
+    640: the fused group kernels + tf32x3 update against the reference's
+    strided loop (experiments/quant_gptq_strided.py:95-133) written in fp64
+    torch with this library's quantizer per block."""
+    import qwantize_b200 as q
+    from qwantize_b200.gptq import _inverse_hessian, gptq
+    from qwantize_b200.synthetic import make_activations, make_weight
+    M, K, bs = 200, 640, 16
+    W = make_weight(M, K, seed=61).float().to(DEV)
+    X = make_activations(2048, K, seed=62, chunk_tokens=1024).to(DEV)
+    H = (X.double().T @ X.double() / X.shape[0]).float()
+    Q, loss = gptq(W, H, fmt, "optimal", bs)
+    Hi = _inverse_hessian(H, 0.01).double()
+    Wr = W.double().clone()
+    Qr = torch.zeros_like(Wr)
+    ref_loss = 0.0
+    fn = getattr(q, f"{fmt}_optimal")
+    for b in range(K // bs):
+        cs, ce = b * bs, (b + 1) * bs
+        wb = Wr[:, cs:ce].float()
+        _, _, dq = fn(wb.reshape(M, 1, bs), return_dequant=True)
+        dq = dq.reshape(M, bs).double()
+        Qr[:, cs:ce] = dq
+        hd = Hi.diagonal()[cs:ce]
+        err = (wb.double() - dq) / hd
+        ref_loss += float(((wb.double() - dq) ** 2 / hd).sum())
+        Wr[:, ce:] -= err @ Hi[cs:ce, ce:]
+    same = (Q.double() == Qr).double().mean().item()
+    assert abs(loss - ref_loss / M) <= 1e-4 * ref_loss / M, (loss, ref_loss / M)
+    assert same >= 0.99, same
