@@ -702,6 +702,28 @@ def extras(ws, rank, device, peak_tf, args):
     return out
 
 
+def profile_call(spec):
+    """Three launches of one quantization of the config-1 weight (native
+    outputs), for ncu captures of a single kernel: spec "fmt,bs,method", e.g.
+    "nvfp4,16,optimal" or "int8,32,optimal"."""
+    from qwantize_b200 import _lib
+    from qwantize_b200.synthetic import make_weight_device
+    fmt, bs, meth = spec.split(",")
+    fmt = {"nvfp4": 0, "mxfp4": 1, "nvint4": 3, "int8": 4}[fmt]
+    bs, meth = int(bs), {"naive": 0, "optimal": 1}[meth]
+    dev = torch.device("cuda", 0)
+    L = _lib.load()
+    W = make_weight_device(M, K, 0, dev)
+    codes = torch.empty(WEIGHTS // bs, dtype=torch.uint8, device=dev)
+    packed = torch.empty(WEIGHTS, dtype=torch.uint8, device=dev)
+    dq = torch.empty(WEIGHTS, dtype=torch.bfloat16, device=dev)
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(3):
+        _lib.check(L.qz_quantize(W.data_ptr(), 1, WEIGHTS // bs, bs, fmt, meth, None, 0, None, None, None,
+                                 codes.data_ptr(), packed.data_ptr(), dq.data_ptr(), sp), "qz_quantize")
+    torch.cuda.synchronize(dev)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -718,8 +740,12 @@ def main():
                     help="layers of the config-4 Llama-3-70B stack (0 skips it)")
     ap.add_argument("--config4-tokens", type=int, default=262144,
                     help="tokens for config 4's full 28672^2 Gram (0 skips it)")
+    ap.add_argument("--profile-call", default=None,
+                    help='only launch one quantization three times (ncu captures), e.g. "int8,32,optimal"')
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile_call:
+        profile_call(args.profile_call)
+    elif args.impl == "reference":
         bench_reference(args)
     else:
         bench_ours(args)
