@@ -222,12 +222,25 @@ QZ_API int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int acc
  *   Hi        (K, K) fp32 damped inverse Hessian; Hi_split 2*K*K fp32 scratch
  *   h_blocks  (K/bs, bs, bs) block Hessians for QZ_METHOD_HESSIAN, else NULL
  *   E         M * 2 * group_cols fp32 scratch
- *   loss      ceil(K / group_cols) * ceil(M / 64) doubles: sum of d^2 / Hi_cc
- *             per (group, 64-row slice); the reference's loss is their sum / M
+ *   loss      ceil(K / group_cols) * ceil(M / 8) doubles: sum of d^2 / Hi_cc
+ *             per (group, 8-row slice); the reference's loss is their sum / M
  */
 QZ_API int qz_gptq(float* Wb, float* Qb, const float* Hi, float* Hi_split, const float* h_blocks, int64_t M,
                    int64_t K, int block_size, int format, int method, int group_cols, float* E, double* loss,
                    void* stream);
+
+/*
+ * qz_spd_inverse -- in-place inverse of a symmetric positive definite fp32
+ * matrix A (n x n, row-major, n a multiple of 32): the damped inverse Hessian
+ * of GPTQ (experiments/quant_gptq_strided.py:72-85 takes it through
+ * torch.linalg.cholesky + cholesky_inverse).  Recursive 2 x 2 blocking on
+ * Schur complements; every product on the tensor cores at fp32 accuracy (tf32
+ * high / low operand pairs), blocks of at most 128 inverted in double
+ * precision.  work: 11 * n * n floats of scratch.  *status (device int) is set
+ * to 1 if a pivot was not positive (A not positive definite; the result is
+ * then not an inverse), else 0.
+ */
+QZ_API int qz_spd_inverse(float* A, int64_t n, float* work, int* status, void* stream);
 
 /*
  * qz_weight_error_sums -- sums[0] += sum (W_dq - W)^2, sums[1] += sum W^2 in

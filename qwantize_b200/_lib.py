@@ -26,7 +26,7 @@ EXPORTS = [
     "qz_quantize", "qz_dequantize", "qz_dequantize_packed", "qz_fp4_unpack", "qz_gram",
     "qz_weight_error_sums", "qz_output_error_sums", "qz_scale_table", "qz_last_error",
     "qz_version", "qz_device_ok", "qz_poll_device_error", "qz_gram_full_noalloc", "qz_admm",
-    "qz_quantize_table", "qz_selftest_wait", "qz_quantize_grouped", "qz_gptq",
+    "qz_quantize_table", "qz_selftest_wait", "qz_quantize_grouped", "qz_gptq", "qz_spd_inverse",
 ]
 
 
@@ -67,6 +67,7 @@ def load():
     L.qz_poll_device_error.argtypes = [i32, vp]
     L.qz_selftest_wait.argtypes = [ctypes.c_uint64, vp]
     L.qz_quantize_grouped.argtypes = [vp, i32, i32, i32, i32, i32, vp]
+    L.qz_spd_inverse.argtypes = [vp, i64, vp, vp, vp]
     L.qz_gptq.argtypes = [vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp]
     L.qz_last_error.restype = ctypes.c_char_p
     for name in EXPORTS:

@@ -214,4 +214,98 @@ cudaError_t launch_split_tf32(const float* src, float* hi, float* lo, int64_t n,
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Pieces of the symmetric-positive-definite inverse (qz_spd_inverse).  Every
+// matrix is fp32 row-major with leading dimension ld; its tf32 high / low
+// split lives in a stacked buffer (high part at S[i], low part at S[i + lo]).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void store_split(float* S, int64_t i, int64_t lo, float v) {
+  uint32_t h, l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(__fsub_rn(v, __uint_as_float(h))));
+  S[i] = __uint_as_float(h);
+  S[i + lo] = __uint_as_float(l);
+}
+
+// In-place inverse of one s x s diagonal block (s <= 128) by Gauss-Jordan
+// elimination without pivoting, in double precision in shared memory (a
+// symmetric positive definite matrix needs no pivoting; a pivot <= 0 means the
+// input is not positive definite: *bad is set and the block is left as is).
+__global__ void __launch_bounds__(256) spd_block_inverse_kernel(float* V, float* S, int64_t ld, int64_t lo, int s,
+                                                                int* bad) {
+  extern __shared__ double A[];  // s x s
+  __shared__ double dinv;
+  for (int i = threadIdx.x; i < s * s; i += blockDim.x) A[i] = (double)V[(i / s) * ld + i % s];
+  __syncthreads();
+  for (int p = 0; p < s; ++p) {
+    if (threadIdx.x == 0) {
+      const double piv = A[p * s + p];
+      if (!(piv > 0.0)) atomicExch(bad, 1);
+      dinv = 1.0 / piv;
+    }
+    __syncthreads();
+    const double d = dinv;
+    // row p scaled; then every other row minus its multiple of row p
+    for (int j = threadIdx.x; j < s; j += blockDim.x)
+      if (j != p) A[p * s + j] *= d;
+    __syncthreads();
+    for (int e = threadIdx.x; e < s * s; e += blockDim.x) {
+      const int i = e / s, j = e % s;
+      if (i != p && j != p) A[e] = fma(-A[i * s + p], A[p * s + j], A[e]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < s; i += blockDim.x)
+      if (i != p) A[i * s + p] = -A[i * s + p] * d;
+    if (threadIdx.x == 0) A[p * s + p] = d;
+    __syncthreads();
+  }
+  if (*bad) return;
+  for (int e = threadIdx.x; e < s * s; e += blockDim.x) {
+    const int i = e / s, j = e % s;
+    // symmetric by construction up to rounding: average the two triangles
+    const float v = (float)(0.5 * (A[e] + A[j * s + i]));
+    V[i * ld + j] = v;
+    store_split(S, i * ld + j, lo, v);
+  }
+}
+
+// dst = sign * src (transposed when trans != 0) for a rows x cols block of src,
+// with dst's split.  32 x 32 tiles through shared memory.
+__global__ void spd_copy_kernel(const float* __restrict__ src, float* dst, float* dst_s, int64_t ld, int64_t lo,
+                                int rows, int cols, float sign, int trans) {
+  __shared__ float t[32][33];
+  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // tile origin in src (col, row)
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = by + k, c = bx + threadIdx.x;
+    if (r < rows && c < cols) t[k][threadIdx.x] = src[(int64_t)r * ld + c];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    int r, c;
+    float v;
+    if (trans) { r = bx + k; c = by + threadIdx.x; v = (r < cols && c < rows) ? t[threadIdx.x][k] : 0.0f;
+                 if (!(r < cols && c < rows)) continue; }
+    else { r = by + k; c = bx + threadIdx.x; if (!(r < rows && c < cols)) continue; v = t[k][threadIdx.x]; }
+    const int64_t i = (int64_t)r * ld + c;
+    const float o = sign < 0.0f ? -v : v;
+    dst[i] = o;
+    store_split(dst_s, i, lo, o);
+  }
+}
+
+cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st) {
+  const int smem = s * s * 8;
+  cudaError_t e = cudaFuncSetAttribute(spd_block_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  spd_block_inverse_kernel<<<1, 256, smem, st>>>(V, S, ld, lo, s, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_spd_copy(const float* src, float* dst, float* dst_s, int64_t ld, int64_t lo, int rows, int cols,
+                            float sign, int trans, cudaStream_t st) {
+  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)), block(32, 8);
+  spd_copy_kernel<<<grid, block, 0, st>>>(src, dst, dst_s, ld, lo, rows, cols, sign, trans);
+  return cudaGetLastError();
+}
+
 }  // namespace qz

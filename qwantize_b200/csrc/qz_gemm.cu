@@ -42,7 +42,12 @@ int current_sms(int* sms);
 constexpr int kGemmThreads = 192;
 constexpr int kBM = 128, kBK = 64;  // tile rows, K-step (64 bf16 = one 128-byte swizzle row)
 
-enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3 };
+enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3, kTf3 = 4 };
+
+// The fp32-accuracy modes: tf32 tensor-core products of high / low operand
+// pairs (kGptq: GPTQ's error update; kTf3: C = beta C + alpha A B for the
+// symmetric-positive-definite inverse).
+__host__ __device__ constexpr bool tf_mode(int mode) { return mode == kGptq || mode == kTf3; }
 
 // Per-mode geometry.  Full Gram / metrics: 128 x 256 tiles, A 16 KB + B 32 KB
 // per stage, 4 stages, two 256-column accumulators (all 512 TMEM columns).
@@ -52,11 +57,11 @@ enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3 };
 // stage holds 32 columns of K (128 bytes per row) of A_hi, A_lo, B_hi, B_lo.
 template <int MODE>
 struct Geo {
-  static constexpr int BN = (MODE == kGramDiag || MODE == kGptq) ? 128 : 256;
-  static constexpr int kABytes = MODE == kGptq ? 2 * kBM * 128 : kBM * kBK * 2;
-  static constexpr int kBBytes = MODE == kGramDiag ? 0 : (MODE == kGptq ? 2 * BN * 128 : BN * kBK * 2);
+  static constexpr int BN = (MODE == kGramDiag || tf_mode(MODE)) ? 128 : 256;
+  static constexpr int kABytes = tf_mode(MODE) ? 2 * kBM * 128 : kBM * kBK * 2;
+  static constexpr int kBBytes = MODE == kGramDiag ? 0 : (tf_mode(MODE) ? 2 * BN * 128 : BN * kBK * 2);
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = MODE == kGramDiag ? 8 : (MODE == kGptq ? 3 : 4);
+  static constexpr int kStages = MODE == kGramDiag ? 8 : (tf_mode(MODE) ? 3 : 4);
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -78,6 +83,18 @@ struct GemmParams {
   // column-block-major working weight Wb (nblk, M, bs)
   float* Wb;
   int64_t g0c, c1, gk;  // group's first column, first column after the group, group width
+  // tf32 modes: the operand tiles of output tile (mi, nj) at K step ks come
+  // from map_a at (a_x0 + 32 ks, a_y0 + 128 mi) (high parts) and (+ a_lo_dx,
+  // + a_lo_dy) (low parts), and likewise from map_b with 128 nj
+  int a_x0, a_y0, a_lo_dx, a_lo_dy, b_x0, b_y0, b_lo_dx, b_lo_dy;
+  // kTf3 output: rows m < p.M, columns n < p.N of C (value, leading dimension
+  // ldc) = alpha acc (+ C if beta); with Cs, its tf32 high part at Cs[i] and
+  // low part at Cs[i + cs_lo]
+  int64_t N, ldc, cs_lo;
+  float* C;
+  float* Cs;
+  float alpha;
+  int beta;
 };
 
 // ---------------------------------------------------------------------------
@@ -178,7 +195,7 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64
     nj = t / p.tiles_m;     // the split index
     return;
   }
-  if (mode == kMetrics || mode == kGptq) {
+  if (mode == kMetrics || tf_mode(mode)) {
     mi = t / p.tiles_n;
     nj = t % p.tiles_n;
     return;
@@ -217,7 +234,7 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t t) {
     u.steps = (p.K + kBK - 1) / kBK;
     return u;
   }
-  if (MODE == kGptq) {
+  if (tf_mode(MODE)) {
     tile_coords(p, MODE, t, u.mi, u.nj);
     u.steps = p.gk / 32;  // 32 fp32 columns (128 bytes) per stage
     return u;
@@ -295,15 +312,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           unsigned char* sa = smem + s * G::kStageBytes;
           unsigned char* sb = sa + G::kABytes;
           mbar_arrive_expect_tx(full + s, G::kStageBytes);
-          if (MODE == kGptq) {
-            // A: the scaled errors (high parts, then low parts, of one row of E);
-            // B: rows c1 + n of Hi (high parts; the low parts are rows K + c1 + n),
-            // columns of the group (Hi is symmetric: B^T = Hi[c1 + n][group])
-            const int kx = (int)(ks * 32), ay = (int)(mi * kBM), by = (int)(p.c1 + nj * 128);
-            tma_load_2d(sa, &map_a, kx, ay, full + s);
-            tma_load_2d(sa + 16384, &map_a, (int)p.gk + kx, ay, full + s);
-            tma_load_2d(sb, &map_b, (int)p.g0c + kx, by, full + s);
-            tma_load_2d(sb + 16384, &map_b, (int)p.g0c + kx, (int)p.K + by, full + s);
+          if (tf_mode(MODE)) {
+            // high and low parts of a 128 x 32 tile of A and of B^T (K-major)
+            const int kx = (int)(ks * 32), ay = p.a_y0 + (int)(mi * kBM), by = p.b_y0 + (int)(nj * 128);
+            tma_load_2d(sa, &map_a, p.a_x0 + kx, ay, full + s);
+            tma_load_2d(sa + 16384, &map_a, p.a_x0 + p.a_lo_dx + kx, ay + p.a_lo_dy, full + s);
+            tma_load_2d(sb, &map_b, p.b_x0 + kx, by, full + s);
+            tma_load_2d(sb + 16384, &map_b, p.b_x0 + p.b_lo_dx + kx, by + p.b_lo_dy, full + s);
           } else if (MODE == kMetrics) {
             const int kx = (int)(ks * kBK);
             tma_load_2d(sa, &map_a, kx, (int)(mi * kBM), full + s);                 // X rows (t)
@@ -333,8 +348,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr bool mn = MODE != kMetrics && MODE != kGptq;
-      constexpr uint32_t idesc = MODE == kGptq ? instr_desc_tf32(kBM, BN) : instr_desc(kBM, BN, mn, mn);
+      constexpr bool mn = MODE != kMetrics && !tf_mode(MODE);
+      constexpr uint32_t idesc = tf_mode(MODE) ? instr_desc_tf32(kBM, BN) : instr_desc(kBM, BN, mn, mn);
       uint32_t it = 0, lt = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
         const int64_t k_steps = unit_of<MODE>(p, t).steps;
@@ -349,7 +364,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * G::kStageBytes);
           const uint32_t sb = MODE == kGramDiag ? sa : sa + G::kABytes;
-          if (MODE == kGptq) {
+          if (tf_mode(MODE)) {
             // D += A_hi B_hi + A_hi B_lo + A_lo B_hi, 8 tf32 (32 bytes) of K per MMA
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -430,6 +445,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float4 w = d4[q];
             w.x -= v[4 * q]; w.y -= v[4 * q + 1]; w.z -= v[4 * q + 2]; w.w -= v[4 * q + 3];
             d4[q] = w;
+          }
+        }
+      } else if (MODE == kTf3) {
+        // C = alpha acc (+ C), and its tf32 high / low split when requested
+        const int64_t r = mi * kBM + row;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          const int64_t c0 = nj * BN + c;
+          if (r >= p.M) continue;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if (c0 + q >= p.N) break;
+            const int64_t i = r * p.ldc + c0 + q;
+            float val = p.alpha * v[q];
+            if (p.beta) val += p.C[i];
+            p.C[i] = val;
+            if (p.Cs) {
+              uint32_t h;
+              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(val));
+              const float hi = __uint_as_float(h);
+              uint32_t l;
+              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(val - hi));
+              p.Cs[i] = hi;
+              p.Cs[i + p.cs_lo] = __uint_as_float(l);
+            }
           }
         }
       } else if (MODE == kGramDiag && p.bs > 32) {
@@ -897,6 +939,11 @@ extern "C" int qz_gptq(float* Wb, float* Qb, const float* Hi, float* Hi_split, c
     GemmParams p{};
     p.M = M; p.K = K; p.bs = bs; p.Wb = Wb;
     p.g0c = g0 * bs; p.c1 = (g0 + gbn) * bs; p.gk = group_cols;
+    // A: the scaled errors (high parts in columns [0, gk), low parts after);
+    // B^T: rows c1 + n of Hi's split copy (high parts; low parts K rows
+    // further), the group's columns (Hi is symmetric)
+    p.a_x0 = 0; p.a_y0 = 0; p.a_lo_dx = group_cols; p.a_lo_dy = 0;
+    p.b_x0 = (int)p.g0c; p.b_y0 = (int)p.c1; p.b_lo_dx = 0; p.b_lo_dy = (int)K;
     p.tiles_m = (M + kBM - 1) / kBM;
     p.tiles_n = (K - p.c1 + 127) / 128;
     p.n_tiles = p.tiles_m * p.tiles_n;
@@ -904,4 +951,104 @@ extern "C" int qz_gptq(float* Wb, float* Qb, const float* Hi, float* Hi_split, c
     if (s != QZ_OK) break;
   }
   return s;
+}
+
+// ---------------------------------------------------------------------------
+// Inverse of a symmetric positive definite matrix by recursive 2 x 2 blocking
+// (Schur complements), every product on the tensor cores at fp32 accuracy
+// (tf32 high / low pairs, three products).  For A = [A11 A12; A21 A22]:
+//   X11 = inv(A11); T = X11 A12; S = A22 - T^T A12; Y = inv(S);
+//   U = T Y; inv(A) = [X11 + U T^T, -U; -U^T, Y].
+// Blocks are multiples of 32 (the K step of the GEMM); blocks of at most 128
+// are inverted directly (Gauss-Jordan in double precision in shared memory).
+// ---------------------------------------------------------------------------
+namespace qz {
+
+struct SpdWork {
+  float* V;    // the matrix (n x n): input, then the inverse
+  float* S;    // its split (2n x n): high part rows [0, n), low part rows [n, 2n)
+  float *T, *Ts, *Tt, *Tts, *U, *Us;  // workspaces: values (n x n) and splits (2n x n)
+  int64_t n;
+  int* bad;
+  CUtensorMap mS, mTs, mTts, mUs;
+  cudaStream_t st;
+};
+
+// C (value at C, split at Cs) = alpha A B (+ C): A = rows [ay, ay + m), columns
+// [ax, ax + k) of the split buffer behind map_a; B^T = rows [by, by + nn),
+// columns [bx, bx + k) of the split buffer behind map_b.
+static int tf3_gemm(const SpdWork& w, const CUtensorMap& ma, int ax, int ay, const CUtensorMap& mb, int bx, int by,
+                    int64_t m, int64_t nn, int64_t k, float* C, float* Cs, float alpha, int beta) {
+  GemmParams p{};
+  p.M = m; p.N = nn; p.gk = k; p.K = w.n;
+  p.a_x0 = ax; p.a_y0 = ay; p.a_lo_dx = 0; p.a_lo_dy = (int)w.n;
+  p.b_x0 = bx; p.b_y0 = by; p.b_lo_dx = 0; p.b_lo_dy = (int)w.n;
+  p.C = C; p.Cs = Cs; p.ldc = w.n; p.cs_lo = w.n * w.n; p.alpha = alpha; p.beta = beta;
+  p.tiles_m = (m + kBM - 1) / kBM;
+  p.tiles_n = (nn + 127) / 128;
+  p.n_tiles = p.tiles_m * p.tiles_n;
+  return launch_gemm<kTf3>(ma, mb, mb, p, w.st);
+}
+
+static int spd_inverse_rec(const SpdWork& w, int64_t off, int64_t s) {
+  const int64_t n = w.n;
+  if (s <= 128)
+    return cuda_status(launch_spd_block_inverse(w.V + off * n + off, w.S + off * n + off, n, n * n, (int)s, w.bad,
+                                                w.st), "spd block inverse");
+  const int64_t s1 = (s / 32 + 1) / 2 * 32, s2 = s - s1, o2 = off + s1;
+  int r = spd_inverse_rec(w, off, s1);  // X11
+  if (r != QZ_OK) return r;
+  // T = X11 A12  (B^T = A12^T = A21: rows o2.., columns off..)
+  r = tf3_gemm(w, w.mS, (int)off, (int)off, w.mS, (int)off, (int)o2, s1, s2, s1, w.T, w.Ts, 1.0f, 0);
+  if (r != QZ_OK) return r;
+  r = cuda_status(launch_spd_copy(w.T, w.Tt, w.Tts, n, n * n, (int)s1, (int)s2, 1.0f, 1, w.st), "spd transpose");
+  if (r != QZ_OK) return r;
+  // S = A22 - T^T A12  (A = T^T: s2 x s1; B^T = A21)
+  float* A22 = w.V + o2 * n + o2;
+  r = tf3_gemm(w, w.mTts, 0, 0, w.mS, (int)off, (int)o2, s2, s2, s1, A22, w.S + o2 * n + o2, -1.0f, 1);
+  if (r != QZ_OK) return r;
+  r = spd_inverse_rec(w, o2, s2);  // Y
+  if (r != QZ_OK) return r;
+  // U = T Y  (B^T = Y, symmetric)
+  r = tf3_gemm(w, w.mTs, 0, 0, w.mS, (int)o2, (int)o2, s1, s2, s2, w.U, w.Us, 1.0f, 0);
+  if (r != QZ_OK) return r;
+  // X11 += U T^T  (B^T = T)
+  r = tf3_gemm(w, w.mUs, 0, 0, w.mTs, 0, 0, s1, s1, s2, w.V + off * n + off, w.S + off * n + off, 1.0f, 1);
+  if (r != QZ_OK) return r;
+  // X12 = -U, X21 = -U^T
+  r = cuda_status(launch_spd_copy(w.U, w.V + off * n + o2, w.S + off * n + o2, n, n * n, (int)s1, (int)s2, -1.0f, 0,
+                                  w.st), "spd copy");
+  if (r != QZ_OK) return r;
+  return cuda_status(launch_spd_copy(w.U, w.V + o2 * n + off, w.S + o2 * n + off, n, n * n, (int)s1, (int)s2, -1.0f,
+                                     1, w.st), "spd transpose");
+}
+
+}  // namespace qz
+
+extern "C" int qz_spd_inverse(float* A, int64_t n, float* work, int* status, void* stream) {
+  if (n <= 0 || n % 32) return fail(QZ_ERR_INVALID, "n must be a positive multiple of 32, got %lld", (long long)n);
+  if (n > 46336) return fail(QZ_ERR_INVALID, "n too large (%lld)", (long long)n);
+  if (!A || !work || !status) return fail(QZ_ERR_INVALID, "NULL pointer");
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(work)) % 16)
+    return fail(QZ_ERR_INVALID, "A and work must be 16-byte aligned");
+  int sms = 0;
+  int r = current_sms(&sms);
+  if (r != QZ_OK) return r;
+  SpdWork w{};
+  w.n = n; w.V = A; w.bad = status; w.st = static_cast<cudaStream_t>(stream);
+  const int64_t nn = n * n;
+  w.S = work;
+  w.T = work + 2 * nn; w.Ts = w.T + nn;
+  w.Tt = w.Ts + 2 * nn; w.Tts = w.Tt + nn;
+  w.U = w.Tts + 2 * nn; w.Us = w.U + nn;
+  r = cuda_status(cudaMemsetAsync(status, 0, sizeof(int), w.st), "cudaMemsetAsync");
+  if (r != QZ_OK) return r;
+  r = cuda_status(launch_split_tf32(A, w.S, w.S + nn, nn, sms, w.st), "split_tf32 launch");
+  if (r != QZ_OK) return r;
+  r = make_map(&w.mS, w.S, (uint64_t)n, (uint64_t)(2 * n), 32, 128, true);
+  if (r == QZ_OK) r = make_map(&w.mTs, w.Ts, (uint64_t)n, (uint64_t)(2 * n), 32, 128, true);
+  if (r == QZ_OK) r = make_map(&w.mTts, w.Tts, (uint64_t)n, (uint64_t)(2 * n), 32, 128, true);
+  if (r == QZ_OK) r = make_map(&w.mUs, w.Us, (uint64_t)n, (uint64_t)(2 * n), 32, 128, true);
+  if (r != QZ_OK) return r;
+  return spd_inverse_rec(w, 0, n);
 }

@@ -61,10 +61,14 @@ struct GptqGroupArgs {
   int g0, gb, gk;         // first column block, blocks in this group, group width in columns (E stride)
 };
 
-constexpr int kGptqRows = 64;  // rows (threads) per CTA of the group kernel
+constexpr int kGptqRows = 8;  // rows (one warp each) per CTA of the group kernel
 
 cudaError_t launch_gptq_group(const GptqGroupArgs& a, int bs, int fmt, int method, cudaStream_t st);
 cudaError_t launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, int num_sms, cudaStream_t st);
+
+cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st);
+cudaError_t launch_spd_copy(const float* src, float* dst, float* dst_s, int64_t ld, int64_t lo, int rows, int cols,
+                            float sign, int trans, cudaStream_t st);
 
 cudaError_t launch_quantize_grouped(const GroupArgs& g, int dtype, int bs, int fmt, int method, int num_sms,
                                     cudaStream_t st);

@@ -1483,19 +1483,21 @@ cudaError_t launch_admm(const QuantArgs& qa, const float* h, const float* hn, co
 }
 
 // ---------------------------------------------------------------------------
-// GPTQ column group (experiments/quant_gptq_strided.py:49-135, gptq_strided):
-// one thread per row of W.  Rows are independent in GPTQ -- a row's later
-// columns depend only on its own earlier errors and the shared inverse
-// Hessian -- so a CTA of kGptqRows threads carries its rows through the whole
-// group: the group's columns live in shared memory (column-major, one word
-// per thread: conflict-free), with Hi's group block beside them (read as
-// broadcasts).  For every column block, left to right:
-//   choose the scale (naive / SSE / Hessian search: the same device code and
-//   arithmetic as qz_quantize on fp32 input), dequantize, d = w - q,
-//   err = d / Hi_cc, loss += d^2 / Hi_cc, and
-//   W[:, later columns of the group] -= err @ Hi[block rows, those columns].
-// The scaled errors leave as a tf32 high / low pair per element for the
-// tensor-core update of the columns after the group (qz_gemm.cu).
+// GPTQ column group (experiments/quant_gptq_strided.py:49-135, gptq_strided).
+// Rows are independent in GPTQ -- a row's later columns depend only on its own
+// earlier errors and the shared inverse Hessian -- so each warp carries one
+// row through the whole group: the row's group columns sit in shared memory,
+// Hi's group block (and, for the Hessian method, the group's H_j) beside them
+// for the CTA's kGptqRows warps.  For every column block, left to right:
+//   scale search with the lanes spread over the candidates (each lane scores
+//   candidates lo + lane, lo + lane + 32, ... with the same device code and
+//   arithmetic as qz_quantize on fp32 input; SSE: minimum of the
+//   (error, index) keys over the warp; Hessian: the reference's sequential
+//   fast-fail scan over the precomputed values), dequantize, d = w - q,
+//   err = d / Hi_cc, loss += d^2 / Hi_cc, then with the lanes over columns
+//   W[later columns of the group] -= err @ Hi[block rows, those columns].
+// The scaled errors leave as tf32 high / low pairs for the tensor-core update
+// of the columns after the group (qz_gemm.cu).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
@@ -1503,10 +1505,21 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-// Scale of one fp32 block, exactly as quantize_kernel (naive, SSE) and
-// hessian_kernel (Hessian; Ht = H_j transposed in shared memory) choose it.
+__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long k) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, k, o);
+    k = t < k ? t : k;
+  }
+  return k;
+}
+
+// Scale of one fp32 block (every lane holds the block), chosen exactly as
+// quantize_kernel (naive, SSE) and hessian_kernel (Hessian; Ht = H_j
+// transposed in shared memory) choose it, with the candidates spread over the
+// warp's lanes.
 template <int BS, int FMT, int METHOD>
-__device__ __forceinline__ float choose_scale_f32(const float (&x)[BS], const float* Ht) {
+__device__ __forceinline__ float choose_scale_warp(const float (&x)[BS], const float* Ht, int lane) {
   constexpr int MODE = Mode<FMT, kDtF32>::v;
   float a[BS];
   const uint32_t amax_bits = abs_and_amax<BS>(x, a);
@@ -1514,117 +1527,111 @@ __device__ __forceinline__ float choose_scale_f32(const float (&x)[BS], const fl
   if (METHOD == kNaive || is_nan_bits(__float_as_uint(s) & 0x7fffffffu)) return s;
   const float E0 = base_sse<BS, MODE, kDtF32, FMT>(a, s);
   int lo, hi;
+  search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
   if constexpr (METHOD == kSSE) {
-    search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
-    float best = E0;
-#pragma unroll 1
-    for (int c = lo; c <= hi; ++c) {
+    // first minimum of the error over [lo, hi], kept only below E0: the
+    // reference's ascending loop with strict '<' (its clipping fast-fail never
+    // changes the winner)
+    unsigned long long key = (unsigned long long)__float_as_uint(E0) << 32;
+    for (int c = lo + lane; c <= hi; c += 32) {
       const float E = cand_sse<BS, MODE, kDtF32, FMT>(a, s_ctab, c);
-      if (E < best) { best = E; s = s_ctab.val[c]; }
+      const unsigned long long k = ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)(c + 1);
+      key = k < key ? k : key;
     }
+    key = warp_min_u64(key);
+    const unsigned win = (unsigned)(key & 0xffffffffu);
+    return win ? s_ctab.val[win - 1] : s;
   } else {
     float best = block_hess_ilp<BS, MODE, kDtF32, FMT>(x, a, s, Ht);
-    search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
-#pragma unroll 1
-    for (int c = lo; c <= hi; ++c) {
-      const float sc = cand_value<FMT>(c);
-      const float Hc = block_clip<BS, FMT>(a, sc);
-      const bool pass = FMT != kMXFP4 ? (Hc < __fmul_rn(best, 10.0f)) : (Hc < E0);
-      if (!pass) continue;
-      const float E = block_hess_ilp<BS, MODE, kDtF32, FMT>(x, a, sc, Ht);
-      if (E < best) { best = E; s = sc; }
+    for (int base = lo; base <= hi; base += 32) {
+      const int c = base + lane;
+      float Hc = 0.0f, E = 0.0f;
+      if (c <= hi) {
+        const float sc = cand_value<FMT>(c);
+        Hc = block_clip<BS, FMT>(a, sc);
+        E = block_hess_ilp<BS, MODE, kDtF32, FMT>(x, a, sc, Ht);
+      }
+      const int n = hi - base + 1 < 32 ? hi - base + 1 : 32;
+      for (int k = 0; k < n; ++k) {  // the reference's sequential scan (nvfp4/reference.py:367-393)
+        const float hk = __shfl_sync(0xffffffffu, Hc, k), ek = __shfl_sync(0xffffffffu, E, k);
+        const bool pass = FMT != kMXFP4 ? (hk < __fmul_rn(best, 10.0f)) : (hk < E0);
+        if (pass && ek < best) { best = ek; s = cand_value<FMT>(base + k); }
+      }
     }
+    return s;
   }
-  return s;
 }
 
 template <int BS, int FMT, int METHOD>
-__global__ void __launch_bounds__(kGptqRows) gptq_group_kernel(GptqGroupArgs A) {
+__global__ void __launch_bounds__(kGptqRows * 32) gptq_group_kernel(GptqGroupArgs A) {
   constexpr int MODE = Mode<FMT, kDtF32>::v;
-  constexpr int R = kGptqRows;
   extern __shared__ __align__(16) float gsm[];
-  const int gc = A.gb * BS;       // columns of this group
+  const int gc = A.gb * BS;  // columns of this group
   const int64_t c0 = (int64_t)A.g0 * BS;
-  float* Hg = gsm;                // gc x gc: Hi[c0 + r][c0 + c]
-  float* Wt = Hg + gc * gc;       // gc x R: column c of this CTA's rows
-  float* hd = Wt + gc * R;        // gc: Hi diagonal
-  float* Ht = hd + gc;            // BS x BS: H_j transposed (Hessian method)
-  __shared__ double red[R / 32];
-  const int t = threadIdx.x;
+  float* Hg = gsm;                    // gc x gc: Hi[c0 + r][c0 + c]
+  float* hd = Hg + gc * gc;           // gc: Hi diagonal
+  float* Hts = hd + gc;               // gb x BS x BS: H_j transposed (Hessian method)
+  float* Wr = Hts + (METHOD == kHessian ? A.gb * BS * BS : 0);  // kGptqRows x gc: the warps' rows
+  __shared__ double red[kGptqRows];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (METHOD != kNaive) fill_cand_table<FMT>(s_ctab);
-  for (int i = t; i < gc * gc; i += R) Hg[i] = A.Hi[(c0 + i / gc) * A.K + c0 + i % gc];
-  for (int i = t; i < gc; i += R) hd[i] = A.Hi[(c0 + i) * A.K + c0 + i];
-  const int64_t m = (int64_t)blockIdx.x * R + t;
-  const bool valid = m < A.M;
-  for (int jj = 0; jj < A.gb; ++jj) {
-    const float4* src = reinterpret_cast<const float4*>(A.Wb + (((int64_t)A.g0 + jj) * A.M + m) * BS);
-#pragma unroll
-    for (int v = 0; v < BS / 4; ++v) {
-      const float4 w = valid ? src[v] : make_float4(0.f, 0.f, 0.f, 0.f);
-      const int c = jj * BS + 4 * v;
-      Wt[(c + 0) * R + t] = w.x;
-      Wt[(c + 1) * R + t] = w.y;
-      Wt[(c + 2) * R + t] = w.z;
-      Wt[(c + 3) * R + t] = w.w;
+  for (int i = threadIdx.x; i < gc * gc; i += blockDim.x) Hg[i] = A.Hi[(c0 + i / gc) * A.K + c0 + i % gc];
+  for (int i = threadIdx.x; i < gc; i += blockDim.x) hd[i] = A.Hi[(c0 + i) * A.K + c0 + i];
+  if (METHOD == kHessian)
+    for (int i = threadIdx.x; i < A.gb * BS * BS; i += blockDim.x) {
+      const int jj = i / (BS * BS), e = i % (BS * BS);
+      Hts[jj * BS * BS + (e % BS) * BS + e / BS] = A.h_blocks[((int64_t)A.g0 + jj) * BS * BS + e];
     }
-  }
+  const int64_t m = (int64_t)blockIdx.x * kGptqRows + warp;
+  const bool valid = m < A.M;
+  float* row = Wr + warp * gc;
+  for (int c = lane; c < gc; c += 32)
+    row[c] = valid ? A.Wb[(((int64_t)A.g0 + c / BS) * A.M + m) * BS + c % BS] : 0.0f;
   __syncthreads();
   double loss = 0.0;
   for (int jj = 0; jj < A.gb; ++jj) {
-    if (METHOD == kHessian) {
-      const float* Hj = A.h_blocks + ((int64_t)A.g0 + jj) * BS * BS;
-      for (int i = t; i < BS * BS; i += R) Ht[(i % BS) * BS + i / BS] = Hj[i];
-      __syncthreads();
-    }
     float x[BS];
 #pragma unroll
-    for (int i = 0; i < BS; ++i) x[i] = Wt[(jj * BS + i) * R + t];
-    const float s = choose_scale_f32<BS, FMT, METHOD>(x, Ht);
+    for (int i = 0; i < BS; ++i) x[i] = row[jj * BS + i];
+    const float s = choose_scale_warp<BS, FMT, METHOD>(x, Hts + jj * BS * BS, lane);
     const bool snan = is_nan_bits(__float_as_uint(s) & 0x7fffffffu);
-    float err[BS], dq[BS];
+    float err[BS];
+    float dq_own = 0.0f, e_own = 0.0f;
 #pragma unroll
     for (int i = 0; i < BS; ++i) {
       // fp4_quantize * s (the generic path of write_block for fp32 input)
       const float q = cb_rt((uint32_t)fp4_index<MODE>(fabsf(x[i]), s));
       const float qs = x[i] > 0.0f ? q : (x[i] < 0.0f ? -q : 0.0f);
-      dq[i] = snan ? s : __fmul_rn(qs, s);
-      const float d = __fsub_rn(x[i], dq[i]);
+      const float dq = snan ? s : __fmul_rn(qs, s);
+      const float d = __fsub_rn(x[i], dq);
       const float h = hd[jj * BS + i];
       err[i] = __fdiv_rn(d, h);
       loss += (double)__fdiv_rn(__fmul_rn(d, d), h);
+      if (i == lane) { dq_own = dq; e_own = err[i]; }
     }
-    if (valid) {
-      float4* dst = reinterpret_cast<float4*>(A.Qb + (((int64_t)A.g0 + jj) * A.M + m) * BS);
-#pragma unroll
-      for (int v = 0; v < BS / 4; ++v) dst[v] = make_float4(dq[4 * v], dq[4 * v + 1], dq[4 * v + 2], dq[4 * v + 3]);
+    if (valid && lane < BS) {
+      A.Qb[(((int64_t)A.g0 + jj) * A.M + m) * BS + lane] = dq_own;
       if (A.E) {
-        float* e = A.E + m * 2 * A.gk + jj * BS;
-#pragma unroll
-        for (int i = 0; i < BS; ++i) {
-          const float hi = tf32_rna(err[i]);
-          e[i] = hi;
-          e[A.gk + i] = tf32_rna(__fsub_rn(err[i], hi));
-        }
+        float* e = A.E + m * 2 * A.gk + jj * BS + lane;
+        const float hi = tf32_rna(e_own);
+        e[0] = hi;
+        e[A.gk] = tf32_rna(__fsub_rn(e_own, hi));
       }
     }
-    // the rest of the group: W[:, c] -= sum_i err_i * Hi[block row i][c]
-#pragma unroll 1
-    for (int c = (jj + 1) * BS; c < gc; ++c) {
+    // the rest of the group: W[c] -= sum_i err_i * Hi[block row i][c]
+    for (int c = (jj + 1) * BS + lane; c < gc; c += 32) {
       float acc = 0.0f;
 #pragma unroll
       for (int i = 0; i < BS; ++i) acc = __fmaf_rn(err[i], Hg[(jj * BS + i) * gc + c], acc);
-      Wt[c * R + t] = __fsub_rn(Wt[c * R + t], acc);
+      row[c] = __fsub_rn(row[c], acc);
     }
-    if (METHOD == kHessian) __syncthreads();  // Ht is rewritten for the next block
+    __syncwarp();
   }
-  if (!valid) loss = 0.0;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) loss += __shfl_xor_sync(0xffffffffu, loss, o);
-  if ((t & 31) == 0) red[t >> 5] = loss;
+  if (lane == 0) red[warp] = valid ? loss : 0.0;
   __syncthreads();
-  if (t == 0) {
+  if (threadIdx.x == 0) {
     double sum = 0.0;
-    for (int w = 0; w < R / 32; ++w) sum += red[w];
+    for (int w = 0; w < kGptqRows; ++w) sum += red[w];
     A.loss[blockIdx.x] = sum;
   }
 }
@@ -1632,12 +1639,13 @@ __global__ void __launch_bounds__(kGptqRows) gptq_group_kernel(GptqGroupArgs A) 
 template <int BS, int FMT, int METHOD>
 static cudaError_t launch_gptq_t(const GptqGroupArgs& a, cudaStream_t st) {
   const int gc = a.gb * BS;
-  const size_t smem = ((size_t)gc * gc + (size_t)gc * kGptqRows + gc + BS * BS) * 4;
+  const size_t smem = ((size_t)gc * gc + gc + (METHOD == kHessian ? (size_t)a.gb * BS * BS : 0) +
+                       (size_t)kGptqRows * gc) * 4;
   cudaError_t e = cudaFuncSetAttribute(gptq_group_kernel<BS, FMT, METHOD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((a.M + kGptqRows - 1) / kGptqRows);
-  gptq_group_kernel<BS, FMT, METHOD><<<grid, kGptqRows, smem, st>>>(a);
+  gptq_group_kernel<BS, FMT, METHOD><<<grid, kGptqRows * 32, smem, st>>>(a);
   return cudaGetLastError();
 }
 

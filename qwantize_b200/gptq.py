@@ -27,17 +27,35 @@ _FMT = {"nvfp4": L.FMT_NVFP4, "mxfp4": L.FMT_MXFP4}
 _METHOD = {"naive": L.METHOD_NAIVE, "optimal": L.METHOD_SSE, "hoptimal": L.METHOD_HESSIAN}
 
 
+def spd_inverse(A: torch.Tensor) -> torch.Tensor:
+    """Inverse of a symmetric positive definite fp32 matrix on the tensor cores
+    (qz_spd_inverse; n a multiple of 32).  Raises torch.linalg.LinAlgError if
+    a pivot is not positive, as torch.linalg.cholesky does."""
+    n = A.shape[0]
+    X = A.to(torch.float32).contiguous().clone()
+    work = torch.empty(11 * n * n, dtype=torch.float32, device=X.device)
+    status = torch.zeros(1, dtype=torch.int32, device=X.device)
+    L.check(L.load().qz_spd_inverse(L.ptr(X), n, L.ptr(work), L.ptr(status), L.stream_ptr(X.device)),
+            "qz_spd_inverse")
+    if int(status.item()):
+        raise torch.linalg.LinAlgError("the matrix is not positive definite")
+    return X
+
+
 def _inverse_hessian(H: torch.Tensor, damp: float) -> torch.Tensor:
-    """Damped H^-1 via Cholesky (experiments/quant_gptq_strided.py:72-85)."""
+    """Damped H^-1 (experiments/quant_gptq_strided.py:72-85): H + damp * mean(diag)
+    I, inverted on the tensor cores when K is a multiple of 32 (through the
+    Cholesky factor otherwise); a matrix that is not positive definite gets
+    the reference's extra 1e-5 * dmu on the diagonal and a second attempt."""
     Hi = H.clone().float()
     dmu = damp * Hi.diagonal().mean()
     Hi.diagonal().add_(dmu)
+    inv = spd_inverse if Hi.shape[0] % 32 == 0 else (lambda A: torch.cholesky_inverse(torch.linalg.cholesky(A)))
     try:
-        Lc = torch.linalg.cholesky(Hi)
+        return inv(Hi).contiguous()
     except torch.linalg.LinAlgError:
         Hi.diagonal().add_(1e-5 * dmu)
-        Lc = torch.linalg.cholesky(Hi)
-    return torch.cholesky_inverse(Lc).contiguous()
+        return inv(Hi).contiguous()
 
 
 def _quant_block(x: torch.Tensor, bs: int, fmt: int, method: int, H_blk, out_dq: torch.Tensor):
@@ -85,7 +103,7 @@ def gptq(W: torch.Tensor, H: torch.Tensor, fmt: str = "nvfp4", method: str = "op
     Hs = torch.empty(2, K, K, dtype=torch.float32, device=dev)
     E = torch.empty(M, 2 * group, dtype=torch.float32, device=dev)
     n_groups = (K + group - 1) // group
-    parts = torch.zeros(n_groups * ((M + 63) // 64), dtype=torch.float64, device=dev)
+    parts = torch.zeros(n_groups * ((M + 7) // 8), dtype=torch.float64, device=dev)
     L.check(L.load().qz_gptq(L.ptr(Wb), L.ptr(Qb), L.ptr(Hi), L.ptr(Hs), L.ptr(H_blocks), M, K, bs, fmt_c,
                              meth_c, group, L.ptr(E), L.ptr(parts), L.stream_ptr(dev)), "qz_gptq")
     Q = Qb.permute(1, 0, 2).reshape(M, K)

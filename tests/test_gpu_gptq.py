@@ -89,3 +89,29 @@ def test_gptq_ragged_rows_vs_strided_loop(fmt):
     same = (Q.double() == Qr).double().mean().item()
     assert abs(loss - ref_loss / M) <= 1e-4 * ref_loss / M, (loss, ref_loss / M)
     assert same >= 0.99, same
+
+
+@pytest.mark.parametrize("n", [32, 128, 160, 416, 1024, 2080])
+def test_spd_inverse_vs_double(n):
+    """qz_spd_inverse (Schur-complement recursion, tf32x3 tensor-core products,
+    double-precision leaf blocks) against the float64 inverse: within the
+    accuracy of an fp32 inverse, |X - X64| <= 1e-5 * cond-scaled max |X64|."""
+    from qwantize_b200.gptq import spd_inverse
+    g = torch.Generator().manual_seed(n)
+    Xa = torch.randn(4 * n, n, generator=g, dtype=torch.float64) * torch.exp(torch.randn(n, generator=g,
+                                                                                          dtype=torch.float64))
+    A = Xa.T @ Xa / (4 * n)
+    A.diagonal().add_(0.01 * A.diagonal().mean())
+    ref = torch.linalg.inv(A)
+    Xi = spd_inverse(A.float().to(DEV)).double().cpu()
+    cond = float(torch.linalg.cond(A))
+    err = float((Xi - ref).abs().max() / ref.abs().max())
+    assert err <= 2e-7 * cond, (err, cond)
+
+
+def test_spd_inverse_rejects_indefinite():
+    from qwantize_b200.gptq import spd_inverse
+    A = torch.eye(64, device=DEV)
+    A[5, 5] = -1.0
+    with pytest.raises(torch.linalg.LinAlgError):
+        spd_inverse(A)
