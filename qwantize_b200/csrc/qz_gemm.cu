@@ -996,31 +996,37 @@ static int spd_inverse_rec(const SpdWork& w, int64_t off, int64_t s) {
     return cuda_status(launch_spd_block_inverse(w.V + off * n + off, w.S + off * n + off, n, n * n, (int)s, w.bad,
                                                 w.st), "spd block inverse");
   const int64_t s1 = (s / 32 + 1) / 2 * 32, s2 = s - s1, o2 = off + s1;
+  // T, T^T and U of this node live in their workspaces at this node's A12 /
+  // A21 positions, which no node below it touches (the first child is done
+  // before T exists; the second child works at rows and columns >= o2)
+  const int64_t p12 = off * n + o2, p21 = o2 * n + off;
   int r = spd_inverse_rec(w, off, s1);  // X11
   if (r != QZ_OK) return r;
   // T = X11 A12  (B^T = A12^T = A21: rows o2.., columns off..)
-  r = tf3_gemm(w, w.mS, (int)off, (int)off, w.mS, (int)off, (int)o2, s1, s2, s1, w.T, w.Ts, 1.0f, 0);
+  r = tf3_gemm(w, w.mS, (int)off, (int)off, w.mS, (int)off, (int)o2, s1, s2, s1, w.T + p12, w.Ts + p12, 1.0f, 0);
   if (r != QZ_OK) return r;
-  r = cuda_status(launch_spd_copy(w.T, w.Tt, w.Tts, n, n * n, (int)s1, (int)s2, 1.0f, 1, w.st), "spd transpose");
+  r = cuda_status(launch_spd_copy(w.T + p12, w.Tt + p21, w.Tts + p21, n, n * n, (int)s1, (int)s2, 1.0f, 1, w.st),
+                  "spd transpose");
   if (r != QZ_OK) return r;
   // S = A22 - T^T A12  (A = T^T: s2 x s1; B^T = A21)
-  float* A22 = w.V + o2 * n + o2;
-  r = tf3_gemm(w, w.mTts, 0, 0, w.mS, (int)off, (int)o2, s2, s2, s1, A22, w.S + o2 * n + o2, -1.0f, 1);
+  r = tf3_gemm(w, w.mTts, (int)off, (int)o2, w.mS, (int)off, (int)o2, s2, s2, s1, w.V + o2 * n + o2,
+               w.S + o2 * n + o2, -1.0f, 1);
   if (r != QZ_OK) return r;
   r = spd_inverse_rec(w, o2, s2);  // Y
   if (r != QZ_OK) return r;
   // U = T Y  (B^T = Y, symmetric)
-  r = tf3_gemm(w, w.mTs, 0, 0, w.mS, (int)o2, (int)o2, s1, s2, s2, w.U, w.Us, 1.0f, 0);
+  r = tf3_gemm(w, w.mTs, (int)o2, (int)off, w.mS, (int)o2, (int)o2, s1, s2, s2, w.U + p12, w.Us + p12, 1.0f, 0);
   if (r != QZ_OK) return r;
   // X11 += U T^T  (B^T = T)
-  r = tf3_gemm(w, w.mUs, 0, 0, w.mTs, 0, 0, s1, s1, s2, w.V + off * n + off, w.S + off * n + off, 1.0f, 1);
+  r = tf3_gemm(w, w.mUs, (int)o2, (int)off, w.mTs, (int)o2, (int)off, s1, s1, s2, w.V + off * n + off,
+               w.S + off * n + off, 1.0f, 1);
   if (r != QZ_OK) return r;
   // X12 = -U, X21 = -U^T
-  r = cuda_status(launch_spd_copy(w.U, w.V + off * n + o2, w.S + off * n + o2, n, n * n, (int)s1, (int)s2, -1.0f, 0,
-                                  w.st), "spd copy");
+  r = cuda_status(launch_spd_copy(w.U + p12, w.V + p12, w.S + p12, n, n * n, (int)s1, (int)s2, -1.0f, 0, w.st),
+                  "spd copy");
   if (r != QZ_OK) return r;
-  return cuda_status(launch_spd_copy(w.U, w.V + o2 * n + off, w.S + o2 * n + off, n, n * n, (int)s1, (int)s2, -1.0f,
-                                     1, w.st), "spd transpose");
+  return cuda_status(launch_spd_copy(w.U + p12, w.V + p21, w.S + p21, n, n * n, (int)s1, (int)s2, -1.0f, 1, w.st),
+                     "spd transpose");
 }
 
 }  // namespace qz
