@@ -227,46 +227,92 @@ __device__ __forceinline__ void store_split(float* S, int64_t i, int64_t lo, flo
   S[i + lo] = __uint_as_float(l);
 }
 
-// In-place inverse of one s x s diagonal block (s <= 128) by Gauss-Jordan
-// elimination without pivoting, in double precision in shared memory (a
+// In-place inverse of one s x s diagonal block (s <= 128, a multiple of 32)
+// by Gauss-Jordan elimination without pivoting, in double precision (a
 // symmetric positive definite matrix needs no pivoting; a pivot <= 0 means the
-// input is not positive definite: *bad is set and the block is left as is).
+// input is not positive definite: *bad is set).  16 x 16 threads, each holding
+// an 8 x 8 set of elements (rows ty + 16a, columns tx + 16b) in registers;
+// per pivot only row p and column p pass through shared memory (two buffers,
+// so one barrier per pivot).
 __global__ void __launch_bounds__(256) spd_block_inverse_kernel(float* V, float* S, int64_t ld, int64_t lo, int s,
                                                                 int* bad) {
-  extern __shared__ double A[];  // s x s
-  __shared__ double dinv;
-  for (int i = threadIdx.x; i < s * s; i += blockDim.x) A[i] = (double)V[(i / s) * ld + i % s];
-  __syncthreads();
+  __shared__ double rowp[2][128], colp[2][128];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  double A[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const int i = ty + 16 * a, j = tx + 16 * b;
+      A[a][b] = (i < s && j < s) ? (double)V[i * ld + j] : (i == j ? 1.0 : 0.0);
+    }
   for (int p = 0; p < s; ++p) {
-    if (threadIdx.x == 0) {
-      const double piv = A[p * s + p];
-      if (!(piv > 0.0)) atomicExch(bad, 1);
-      dinv = 1.0 / piv;
+    const int buf = p & 1, pa = p >> 4, pr = p & 15;
+    if (ty == pr) {
+#pragma unroll
+      for (int b = 0; b < 8; ++b) if (b * 16 + tx < 128) {
+        double v = 0.0;
+#pragma unroll
+        for (int a = 0; a < 8; ++a) v = a == pa ? A[a][b] : v;
+        rowp[buf][tx + 16 * b] = v;
+      }
+    }
+    if (tx == pr) {
+#pragma unroll
+      for (int a = 0; a < 8; ++a) {
+        double v = 0.0;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) v = b == pa ? A[a][b] : v;
+        colp[buf][ty + 16 * a] = v;
+      }
     }
     __syncthreads();
-    const double d = dinv;
-    // row p scaled; then every other row minus its multiple of row p
-    for (int j = threadIdx.x; j < s; j += blockDim.x)
-      if (j != p) A[p * s + j] *= d;
-    __syncthreads();
-    for (int e = threadIdx.x; e < s * s; e += blockDim.x) {
-      const int i = e / s, j = e % s;
-      if (i != p && j != p) A[e] = fma(-A[i * s + p], A[p * s + j], A[e]);
+    const double piv = rowp[buf][p];
+    if (threadIdx.x == 0 && !(piv > 0.0)) atomicExch(bad, 1);
+    const double d = 1.0 / piv;
+    double rj[8], fi[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) rj[b] = rowp[buf][tx + 16 * b];
+#pragma unroll
+    for (int a = 0; a < 8; ++a) fi[a] = colp[buf][ty + 16 * a] * d;
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) A[a][b] = fma(-fi[a], rj[b], A[a][b]);
+    // row p, column p and the pivot itself
+    if (ty == pr) {
+#pragma unroll
+      for (int a = 0; a < 8; ++a)
+        if (a == pa)
+#pragma unroll
+          for (int b = 0; b < 8; ++b) A[a][b] = rj[b] * d;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < s; i += blockDim.x)
-      if (i != p) A[i * s + p] = -A[i * s + p] * d;
-    if (threadIdx.x == 0) A[p * s + p] = d;
-    __syncthreads();
+    if (tx == pr) {
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
+        if (b == pa)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) A[a][b] = (ty + 16 * a == p) ? d : -fi[a];
+    }
   }
-  if (*bad) return;
-  for (int e = threadIdx.x; e < s * s; e += blockDim.x) {
-    const int i = e / s, j = e % s;
-    // symmetric by construction up to rounding: average the two triangles
-    const float v = (float)(0.5 * (A[e] + A[j * s + i]));
-    V[i * ld + j] = v;
-    store_split(S, i * ld + j, lo, v);
-  }
+  // symmetric by construction up to rounding: average the two triangles
+  extern __shared__ float tr[];  // 128 x 129
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) tr[(ty + 16 * a) * 129 + tx + 16 * b] = (float)A[a][b];
+  __syncthreads();
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const int i = ty + 16 * a, j = tx + 16 * b;
+      if (i < s && j < s) {
+        const float v = (float)(0.5 * (A[a][b] + (double)tr[j * 129 + i]));
+        V[i * ld + j] = v;
+        store_split(S, i * ld + j, lo, v);
+      }
+    }
 }
 
 // dst = sign * src (transposed when trans != 0) for a rows x cols block of src,
@@ -294,7 +340,7 @@ __global__ void spd_copy_kernel(const float* __restrict__ src, float* dst, float
 }
 
 cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st) {
-  const int smem = s * s * 8;
+  const int smem = 128 * 129 * 4;
   cudaError_t e = cudaFuncSetAttribute(spd_block_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   spd_block_inverse_kernel<<<1, 256, smem, st>>>(V, S, ld, lo, s, bad);

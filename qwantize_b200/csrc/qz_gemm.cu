@@ -448,29 +448,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else if (MODE == kTf3) {
-        // C = alpha acc (+ C), and its tf32 high / low split when requested
+        // C = alpha acc (+ C), and its tf32 high / low split when requested;
+        // 16 consecutive columns per chunk (M, N, ldc and the block offsets
+        // are multiples of 32, so chunks are whole and 16-byte aligned)
         const int64_t r = mi * kBM + row;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
           float v[16];
           tmem_ld16(taddr + c, v);
           const int64_t c0 = nj * BN + c;
-          if (r >= p.M) continue;
+          if (r >= p.M || c0 >= p.N) continue;
+          float4* cp = reinterpret_cast<float4*>(p.C + r * p.ldc + c0);
+          float o[16];
+          if (p.beta) {
+            float4 t[4];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            if (c0 + q >= p.N) break;
-            const int64_t i = r * p.ldc + c0 + q;
-            float val = p.alpha * v[q];
-            if (p.beta) val += p.C[i];
-            p.C[i] = val;
-            if (p.Cs) {
-              uint32_t h;
-              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(val));
-              const float hi = __uint_as_float(h);
-              uint32_t l;
-              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(val - hi));
-              p.Cs[i] = hi;
-              p.Cs[i + p.cs_lo] = __uint_as_float(l);
+            for (int q = 0; q < 4; ++q) t[q] = cp[q];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              o[4 * q] = fmaf(p.alpha, v[4 * q], t[q].x);
+              o[4 * q + 1] = fmaf(p.alpha, v[4 * q + 1], t[q].y);
+              o[4 * q + 2] = fmaf(p.alpha, v[4 * q + 2], t[q].z);
+              o[4 * q + 3] = fmaf(p.alpha, v[4 * q + 3], t[q].w);
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) o[q] = p.alpha * v[q];
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) cp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          if (p.Cs) {
+            float hi[16], lo[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              uint32_t h, l;
+              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(o[q]));
+              hi[q] = __uint_as_float(h);
+              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(o[q] - hi[q]));
+              lo[q] = __uint_as_float(l);
+            }
+            float4* hp = reinterpret_cast<float4*>(p.Cs + r * p.ldc + c0);
+            float4* lp = reinterpret_cast<float4*>(p.Cs + p.cs_lo + r * p.ldc + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              hp[q] = make_float4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
+              lp[q] = make_float4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
             }
           }
         }
