@@ -635,284 +635,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Full Gram on CTA pairs (cta_group::2).  A cluster of two CTAs computes a
-// 256 x 256 tile of H: each CTA loads its own 128 columns of X for the A side
-// (rows of H) and its own 128 of the B side (columns of H), 32 KB per 64-token
-// stage instead of 48 KB for a 128 x 256 tile on one CTA, and the even CTA
-// issues tcgen05.mma.cta_group::2 (M = 256, N = 256) over both CTAs' shared
-// memory into both CTAs' tensor memory (each holds its 128 rows x 256
-// columns).  Loads carry no multicast: each CTA reads only its own panels, and
-// the odd CTA's copies complete on the even CTA's barrier.  The epilogue of
-// each CTA is the one-CTA epilogue for its 128 rows.
-// ---------------------------------------------------------------------------
-constexpr int kG2Stages = 6;
-constexpr int kG2StageBytes = 32768;  // A 16 KB + B 16 KB per CTA
-constexpr int kG2Smem = kG2Stages * kG2StageBytes + 1024 + 256;
-constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // shared::cluster address of the even CTA's copy
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-      "[%4];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar) & kPeerMask)
-      : "memory");
-}
-__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// arrive on `bar` in both CTAs of the pair once the issued MMAs are done
-__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
-  asm volatile(
-      "{\n .reg .b16 m;\n mov.b16 m, 3;\n"
-      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}\n" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-// arrive on the even CTA's copy of `bar`
-__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(smem_u32(bar) & kPeerMask)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// Pair tile t of the upper triangle: (mi2, nj) in 256-blocks with nj >= mi2,
-// enumerated in bands of p.band pair rows, column by column inside a band.
-__device__ __forceinline__ void pair_coords(const GemmParams& p, int64_t t, int64_t& mi2, int64_t& nj) {
-  int64_t r = t;
-  for (int64_t b0 = 0; b0 < p.tiles_m; b0 += p.band) {
-    const int64_t rows_end = b0 + p.band < p.tiles_m ? b0 + p.band : p.tiles_m;
-    for (int64_t n = b0; n < p.tiles_n; ++n) {
-      const int64_t hi = rows_end < n + 1 ? rows_end : n + 1;  // rows with mi2 <= n
-      const int64_t cnt = hi - b0;
-      if (r < cnt) { mi2 = b0 + r; nj = n; return; }
-      r -= cnt;
-    }
-  }
-  mi2 = nj = 0;
-}
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
-    gram_pair_kernel(const __grid_constant__ CUtensorMap map_x, GemmParams p) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kG2Stages * kG2StageBytes);
-  uint64_t* empty = full + kG2Stages;
-  uint64_t* tfull = empty + kG2Stages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
-  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_base_s + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const bool leader = rank == 0;
-  const int64_t cl = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kG2Stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 256); }  // both CTAs' epilogues
-    mbar_init(mma_done, 1);
-    *abort_s = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) tmem_alloc_pair(tmem_base_s, 512);
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // the peer's barriers exist before any copy or arrive targets them
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_base_s;
-
-  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned err) -> bool {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-      if (*abort_s) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        atomicOr(&qz_device_error, err);
-        *abort_s = 1;
-        return false;
-      }
-    }
-    return true;
-  };
-  auto unit = [&](int64_t t, int64_t& mi2, int64_t& nj, int64_t& r0, int64_t& steps, int64_t& tile, int64_t& seg) {
-    seg = t / p.tiles_per_seg;
-    tile = t % p.tiles_per_seg;
-    pair_coords(p, tile, mi2, nj);
-    r0 = seg * p.seg_rows;
-    const int64_t r1 = r0 + p.seg_rows < p.T ? r0 + p.seg_rows : p.T;
-    steps = (r1 - r0 + kBK - 1) / kBK;
-  };
-
-  if (warp == 0) {
-    // ---------------- TMA producer (both CTAs) ----------------
-    if (lane == 0) {
-      uint32_t it = 0;
-      for (int64_t t = cl; t < p.n_tiles; t += ncl) {
-        int64_t mi2, nj, r0, steps, tile, seg;
-        unit(t, mi2, nj, r0, steps, tile, seg);
-        const int xa = (int)(mi2 * 256 + rank * 128), xb = (int)(nj * 256 + rank * 128);
-        for (int64_t ks = 0; ks < steps; ++ks, ++it) {
-          const int s = it % kG2Stages;
-          if (!wait(empty + s, ((it / kG2Stages) & 1) ^ 1, kDevErrLoadTimeout)) goto producer_done;
-          unsigned char* sa = smem + s * kG2StageBytes;
-          unsigned char* sb = sa + 16384;
-          if (leader) mbar_arrive_expect_tx(full + s, 2 * kG2StageBytes);  // both CTAs' bytes
-          const int ty = (int)(r0 + ks * kBK);
-          tma_load_2d_pair(sa, &map_x, xa, ty, full + s);
-          tma_load_2d_pair(sa + 8192, &map_x, xa + 64, ty, full + s);
-          tma_load_2d_pair(sb, &map_x, xb, ty, full + s);
-          tma_load_2d_pair(sb + 8192, &map_x, xb + 64, ty, full + s);
-        }
-      }
-    producer_done:
-      // the even CTA waits, bounded, for the last copies into each stage (the
-      // odd CTA's copies complete on the even CTA's barriers)
-      if (leader)
-        for (uint32_t k = it > (uint32_t)kG2Stages ? it - kG2Stages : 0u; k < it; ++k)
-          mbar_wait_bounded(full + (k % kG2Stages), (k / kG2Stages) & 1, kDevErrLoadTimeout);
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer (even CTA) ----------------
-    if (leader && lane == 0) {
-      constexpr uint32_t idesc = instr_desc(256, 256, true, true);
-      uint32_t it = 0, lt = 0;
-      for (int64_t t = cl; t < p.n_tiles; t += ncl, ++lt) {
-        int64_t mi2, nj, r0, steps, tile, seg;
-        unit(t, mi2, nj, r0, steps, tile, seg);
-        const uint32_t acc = lt & 1;
-        if (!wait(tempty + acc, ((lt >> 1) & 1) ^ 1, kDevErrMmaTimeout)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * 256;
-        bool ok = true;
-        for (int64_t ks = 0; ks < steps; ++ks, ++it) {
-          const int s = it % kG2Stages;
-          if (!wait(full + s, (it / kG2Stages) & 1, kDevErrMmaTimeout)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * kG2StageBytes), sb = sa + 16384;
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16_pair(d_tmem, smem_desc(sa + kk * 2048, p.lbo, p.sbo), smem_desc(sb + kk * 2048, p.lbo, p.sbo),
-                           idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-          umma_commit_pair_both(empty + s);
-        }
-        if (!ok) break;
-        umma_commit_pair_both(tfull + acc);
-      }
-      umma_commit_pair(mma_done);
-      mbar_wait_bounded(mma_done, 0u, kDevErrMmaTimeout);
-    }
-  } else {
-    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    uint32_t lt = 0;
-    for (int64_t t = cl; t < p.n_tiles; t += ncl, ++lt) {
-      int64_t mi2, nj, r0, steps, tile, seg;
-      unit(t, mi2, nj, r0, steps, tile, seg);
-      const uint32_t acc = lt & 1;
-      if (!wait(tfull + acc, (lt >> 1) & 1, kDevErrEpilogueTimeout)) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
-      // this CTA's half of the tile: counters per (tile, half), segments in order
-      int* seqp = p.seq + 2 * tile + rank;
-      bool go = true;
-      if (lane == 0) {
-        const volatile int* sq = seqp;
-        if (*sq < seg) {
-          const uint64_t t0 = globaltimer_ns();
-          while (*sq < seg) {
-            if (*abort_s) { go = false; break; }
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-              atomicOr(&qz_device_error, kDevErrEpilogueTimeout);
-              *abort_s = 1;
-              go = false;
-              break;
-            }
-            __nanosleep(256);
-          }
-        }
-      }
-      go = __shfl_sync(0xffffffffu, go, 0);
-      if (!go) break;
-      __threadfence();
-      const bool add = seg > 0 || p.accumulate;
-      const int64_t i = (mi2 * 2 + rank) * kBM + row;
-      const int64_t j0 = nj * 256;
-#pragma unroll 1
-      for (int c = 0; c < 256; c += 16) {
-        float v[16];
-        tmem_ld16(taddr + c, v);
-        if (i >= p.K) continue;
-        const int64_t jc = j0 + c;
-        if (jc >= i + 1 && jc + 16 <= p.K) {
-          float4* up = reinterpret_cast<float4*>(p.H + i * p.K + jc);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            if (add) {
-              const float4 o = up[q];
-              w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
-            }
-            up[q] = w;
-            v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
-          }
-#pragma unroll
-          for (int q = 0; q < 16; ++q) p.H[(jc + q) * p.K + i] = v[q];
-        } else {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const int64_t j = jc + q;
-            if (j >= p.K || j < i) continue;
-            float* up = p.H + i * p.K + j;
-            const float val = add ? v[q] + *up : v[q];
-            *up = val;
-            if (j > i) p.H[j * p.K + i] = val;
-          }
-        }
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (warp == 2 && lane == 0) atomicExch(seqp, (int)(seg + 1));
-      tc_fence_before();
-      mbar_arrive_leader(tempty + acc);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // no CTA leaves while its peer may still signal its barriers or use its TMEM
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem_base, 512);
-  }
-}
-
 // H += partials[0] + partials[1] + ... in a fixed order (deterministic).
 __global__ void add_partials_kernel(float4* __restrict__ H, const float4* __restrict__ parts, int64_t n4,
                                     int64_t n_parts) {
@@ -1069,35 +791,29 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   int s = current_sms(&sms);
   if (s != QZ_OK) return s;
   if (mode == QZ_GRAM_FULL) {
-    // One persistent launch of CTA pairs over (segment, 256 x 256 tile) units,
-    // segment-major: all pairs sweep the same token rows at about the same
-    // time, so the column panels they share stay in L2.  Each half-tile's
-    // segments are added in segment order (per-half counters in scratch), so
-    // H is deterministic and exactly symmetric.
-    p.tiles_m = p.tiles_n = (K + 255) / 256;
-    const int64_t n = p.tiles_m * (p.tiles_m + 1) / 2;
+    // One persistent launch over (segment, tile) units, segment-major: all CTAs
+    // sweep the same token rows at about the same time, so the column panels
+    // they share stay in L2.  A tile's segments are added in segment order
+    // (per-tile counters in scratch), so H is deterministic and exactly symmetric.
+    p.tiles_n = (K + 255) / 256;
+    int64_t n = 0;
+    for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
     p.tiles_per_seg = n;
     p.seg_rows = kGramSegmentRows;
     const int64_t n_segs = (T + p.seg_rows - 1) / p.seg_rows;
     p.n_tiles = n * n_segs;
-    p.band = 2;
+    p.band = kGramBand;
     p.T = T;
     p.accumulate = accumulate;
     CUtensorMap map;
     s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);
     if (s != QZ_OK) return s;
     int* seq = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&seq), (size_t)(2 * n) * sizeof(int), st);
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&seq), (size_t)n * sizeof(int), st);
     if (e != cudaSuccess) return cuda_status(e, "cudaMallocAsync (gram tile counters)");
-    e = cudaMemsetAsync(seq, 0, (size_t)(2 * n) * sizeof(int), st);
+    e = cudaMemsetAsync(seq, 0, (size_t)n * sizeof(int), st);
     p.seq = seq;
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gram_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kG2Smem);
-    if (e == cudaSuccess) {
-      const int64_t pairs = p.n_tiles < sms / 2 ? p.n_tiles : sms / 2;
-      gram_pair_kernel<<<(unsigned)(2 * pairs), kGemmThreads, kG2Smem, st>>>(map, p);
-      e = cudaGetLastError();
-    }
-    s = cuda_status(e, "gram pair launch");
+    s = e == cudaSuccess ? launch_gemm<kGramFull>(map, map, map, p, st) : cuda_status(e, "cudaMemsetAsync");
     cudaFreeAsync(seq, st);
     return s;
   }
