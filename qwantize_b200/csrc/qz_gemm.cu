@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * G::kStageBytes);
           const uint32_t sb = MODE == kGramDiag ? sa : sa + G::kABytes;
-          if (tf_mode(MODE)) {
+          if constexpr (tf_mode(MODE)) {
             // D += A_hi B_hi + A_hi B_lo + A_lo B_hi, 8 tf32 (32 bytes) of K per MMA
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -374,20 +374,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               umma_tf32(d_tmem, ah, bl, idesc, 1u);
               umma_tf32(d_tmem, ah, bh, idesc, 1u);
             }
-            umma_commit(empty + s);
-            continue;
-          }
+          } else {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            uint64_t ad, bd;
-            if (mn) {  // MN-major: a 16-row K step is two 8-row swizzle atoms (2 KB)
-              ad = smem_desc(sa + kk * 2048, p.lbo, p.sbo);
-              bd = smem_desc(sb + kk * 2048, p.lbo, p.sbo);
-            } else {   // K-major: 16 elements = 32 bytes inside the 128-byte swizzle row
-              ad = smem_desc(sa + kk * 32, 16, 1024);
-              bd = smem_desc(sb + kk * 32, 16, 1024);
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              uint64_t ad, bd;
+              if (mn) {  // MN-major: a 16-row K step is two 8-row swizzle atoms (2 KB)
+                ad = smem_desc(sa + kk * 2048, p.lbo, p.sbo);
+                bd = smem_desc(sb + kk * 2048, p.lbo, p.sbo);
+              } else {   // K-major: 16 elements = 32 bytes inside the 128-byte swizzle row
+                ad = smem_desc(sa + kk * 32, 16, 1024);
+                bd = smem_desc(sb + kk * 32, 16, 1024);
+              }
+              umma_bf16(d_tmem, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
             }
-            umma_bf16(d_tmem, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(empty + s);
         }
