@@ -36,6 +36,20 @@ __device__ __forceinline__ constexpr float cbv(int k) {
        : k == 4 ? 2.0f : k == 5 ? 3.0f : k == 6 ? 4.0f : 6.0f;
 }
 
+// fl32(a / s) > B_k without dividing, for a >= 0 and a finite s > 0:
+// the boundaries have at most 3 significant bits, so the fp32 midpoint just
+// above B_k is B_k + ulp(B_k) / 2 and a tie there rounds (to even) down to
+// B_k; hence fl(a / s) > B_k  <=>  a / s > B_k + ulp / 2  <=>  a > s * (B_k +
+// ulp / 2), a product that is exact in double (<= 24 + 24 significant bits)
+// and, for fp32 a, the same test as a > RD_fp32(that product).
+__device__ __forceinline__ constexpr double bnd_mid(int k) {
+  return k == 0 ? 0.25 + 0x1p-26 : k == 1 ? 0.75 + 0x1p-25 : k == 2 ? 1.25 + 0x1p-24 : k == 3 ? 1.75 + 0x1p-24
+       : k == 4 ? 2.5 + 0x1p-23 : k == 5 ? 3.5 + 0x1p-23 : 5.0 + 0x1p-22;
+}
+__device__ __forceinline__ float div_threshold(float s, int k) {
+  return __double2float_rd(__dmul_rn((double)s, bnd_mid(k)));
+}
+
 // Codebook value of a runtime index 0..7 without a table or branches:
 // for c >= 2 the E2M1 value 2^((c>>1)-1) * (1 + (c&1)/2) has fp32 bits
 // (c << 22) + 0x3f000000; c = 1 is 0.5 and c = 0 is 0.

@@ -52,17 +52,21 @@ struct FastQ {
 #pragma unroll
     for (int k = 0; k < 7; ++k) {
       if (MODE == kCmp) T[k] = __fmul_rn(bnd(k), s_);
+      // the IEEE quotient's decisions as thresholds (s = 0 gives thresholds 0:
+      // every decision fails for a = 0 or NaN, passes for a > 0 -- dequant 0
+      // either way, as with the quotient)
+      if (MODE == kDiv) T[k] = div_threshold(s_, k);
       V[k] = __fmul_rn(cbv(k + 1), s_);
     }
     r = MODE == kRcp ? __frcp_rn(s_) : 0.0f;
   }
   __device__ __forceinline__ float operator()(float a) const {
     float t = 0.0f;
-    if (MODE == kCmp) {
+    if (MODE == kCmp || MODE == kDiv) {
 #pragma unroll
       for (int k = 0; k < 7; ++k) t = (a > T[k]) ? V[k] : t;
     } else {
-      float y = MODE == kDiv ? __fdiv_rn(a, s) : __fmul_rn(a, r);
+      float y = __fmul_rn(a, r);
 #pragma unroll
       for (int k = 0; k < 7; ++k) t = (y > bnd(k)) ? V[k] : t;
     }
@@ -77,6 +81,9 @@ __device__ __forceinline__ int fp4_index(float a, float s) {
   if (MODE == kCmp) {
 #pragma unroll
     for (int k = 0; k < 7; ++k) idx += (a <= __fmul_rn(bnd(k), s)) ? 0 : 1;
+  } else if (MODE == kDiv && s > 0.0f && __float_as_uint(s) < 0x7f800000u && a == a) {
+#pragma unroll
+    for (int k = 0; k < 7; ++k) idx += (a > div_threshold(s, k)) ? 1 : 0;
   } else {
     float y = MODE == kDiv ? __fdiv_rn(a, s) : __fmul_rn(a, __frcp_rn(s));
 #pragma unroll

@@ -48,3 +48,37 @@ def test_biased_hardware_rounding_equals_bucketize(kind):
         assert not tie.any(), float(s)
         ref = _ref_bucket(a, s)
         assert np.array_equal(got, ref), (kind, float(s), int((got != ref).sum()))
+
+
+MID = np.array([0.25 + 2.0 ** -26, 0.75 + 2.0 ** -25, 1.25 + 2.0 ** -24, 1.75 + 2.0 ** -24, 2.5 + 2.0 ** -23,
+                3.5 + 2.0 ** -23, 5.0 + 2.0 ** -22], np.float64)
+
+
+def _rd32(x):
+    """Round float64 toward -inf to float32."""
+    f = x.astype(np.float32)
+    return np.where(f.astype(np.float64) > x, np.nextafter(f, np.float32(-np.inf)), f)
+
+
+def test_division_free_bucketize_for_fp32_input():
+    """fp32 inputs: fl32(a / s) > B_k  <=>  a > RD32(s * (B_k + ulp(B_k) / 2)).
+    Checked against the IEEE quotient for every E4M3 / UE8M0 scale and random
+    fp32 table scales, over random fp32 magnitudes plus, for each scale, the
+    floats next to every threshold (where the two tests could disagree)."""
+    nv, mx = _scales()
+    g = np.random.default_rng(3)
+    tab = np.sort(np.exp(g.uniform(-30, 30, 400))).astype(np.float32)
+    for s in np.concatenate([nv, mx[(mx > 1e-30) & (mx < 1e30)], tab]):
+        s = np.float32(s)
+        T = _rd32(np.float64(s) * MID)
+        a = np.concatenate([
+            (np.exp(g.uniform(-12, 3, 4000)) * s).astype(np.float32),
+            T, np.nextafter(T, np.float32(np.inf)), np.nextafter(T, np.float32(0)),
+            (B.astype(np.float64) * s).astype(np.float32),
+        ]).astype(np.float32)
+        a = a[np.isfinite(a)]
+        with np.errstate(over="ignore"):
+            q = (a / s).astype(np.float32)
+        want = (q[:, None] > B[None, :])
+        got = (a[:, None] > T[None, :])
+        assert np.array_equal(want, got), float(s)
