@@ -708,6 +708,17 @@ def profile_call(spec):
     "nvfp4,16,optimal" or "int8,32,optimal"."""
     from qwantize_b200 import _lib
     from qwantize_b200.synthetic import make_weight_device
+    if spec == "gptq":  # one GPTQ run: NVFP4 bs16 SSE-optimal, H from 65,536 tokens
+        from qwantize_b200.gptq import gptq
+        from qwantize_b200.hessian import gram
+        from qwantize_b200.synthetic import make_activations
+        dev = torch.device("cuda", 0)
+        X = make_activations(65536, K, seed=1, device=dev)
+        H = gram(X, "full") / 65536
+        del X
+        gptq(make_weight_device(M, K, 0, dev), H, "nvfp4", "optimal", 16)
+        torch.cuda.synchronize(dev)
+        return
     fmt, bs, meth = spec.split(",")
     fmt = {"nvfp4": 0, "mxfp4": 1, "nvint4": 3, "int8": 4}[fmt]
     bs, meth = int(bs), {"naive": 0, "optimal": 1}[meth]
@@ -741,7 +752,8 @@ def main():
     ap.add_argument("--config4-tokens", type=int, default=262144,
                     help="tokens for config 4's full 28672^2 Gram (0 skips it)")
     ap.add_argument("--profile-call", default=None,
-                    help='only launch one quantization three times (ncu captures), e.g. "int8,32,optimal"')
+                    help='only launch one quantization three times (ncu captures), e.g. "int8,32,optimal"; '
+                         '"gptq" runs one GPTQ of the config weight')
     args = ap.parse_args()
     if args.profile_call:
         profile_call(args.profile_call)
