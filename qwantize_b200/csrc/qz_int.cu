@@ -93,36 +93,16 @@ __device__ __forceinline__ float int_dq(float q, float s) {
 
 // Block SSE for a finite scale s >= 0 or NaN (compute_block_sse,
 // nvint4/reference.py:50-56, int8/reference.py:68-83).
-// For a finite s > 0 (fast) the quotient is replaced by y = a * RN(1/s): below
-// 128 it lies within 2^-15.4 of fl(a / s), so both round to the same integer
-// unless y is within 2^-14 of a half integer -- then (rarely) the lane redoes
-// its elements with the IEEE quotient.  Round half to even by the 1.5 * 2^23
-// add / subtract; NaN and inf propagate as through the quotient.
 template <int BS, int FMT, int DT>
 __device__ __forceinline__ float int_sse(const float (&x)[BS / 8], float s, float rc, bool fast) {
   float d2[BS / 8];
-  bool near = !fast;
-  if (fast) {
 #pragma unroll
-    for (int j = 0; j < BS / 8; ++j) {  // on |x| (the SSE is sign-symmetric); NaN propagates
-      const float a = fabsf(x[j]);
-      const float y = __fmul_rn(a, rc);
-      const float q = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
-      near |= fabsf(fabsf(__fsub_rn(y, q)) - 0.5f) <= 0x1p-14f;
-      const float qc = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
-      const float d = __fsub_rn(a, __fmul_rn(qc, s));
-      d2[j] = __fmul_rn(d, d);
-    }
-  }
-  if (near) {
-#pragma unroll
-    for (int j = 0; j < BS / 8; ++j) {
-      const float a = fabsf(x[j]);
-      const float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
-      const float qc = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
-      const float d = __fsub_rn(a, __fmul_rn(qc, s));
-      d2[j] = __fmul_rn(d, d);
-    }
+  for (int j = 0; j < BS / 8; ++j) {  // on |x| (the SSE is sign-symmetric); NaN propagates
+    const float a = fabsf(x[j]);
+    const float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
+    const float qc = q > IntQ<FMT>::v ? IntQ<FMT>::v : q;
+    const float d = __fsub_rn(a, __fmul_rn(qc, s));
+    d2[j] = __fmul_rn(d, d);
   }
   return group_sum<BS>(d2);
 }

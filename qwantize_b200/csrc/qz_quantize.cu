@@ -320,28 +320,17 @@ __device__ __noinline__ float int8_round_div(float a, float s) {
 template <int BS>
 __device__ __forceinline__ float int8_sse(const float (&a)[BS], float s, float rc) {
   float d2[BS];
-  bool near = false;
 #pragma unroll
   for (int i = 0; i < BS; ++i) {
     // a * RN(1/s) is within 2^-15.4 of fl(a / s) below 128, so its rounding
-    // agrees unless it lies within 2^-14 of a half integer: then (rarely) the
-    // block is redone with the IEEE quotient (s = 0 gives inf / NaN either
-    // way; above 128 both clamp)
+    // agrees unless it lies within 2^-14 of a half integer: then the quotient
+    // decides (s = 0 gives inf / NaN either way; above 128 both clamp)
     const float y = __fmul_rn(a[i], rc);
     float q = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
-    near |= fabsf(fabsf(__fsub_rn(y, q)) - 0.5f) <= 0x1p-14f;
+    if (fabsf(fabsf(__fsub_rn(y, q)) - 0.5f) <= 0x1p-14f) q = int8_round_div(a[i], s);
     q = q > 127.0f ? 127.0f : q;
     const float d = __fsub_rn(a[i], __fmul_rn(q, s));
     d2[i] = __fmul_rn(d, d);
-  }
-  if (near) {
-#pragma unroll
-    for (int i = 0; i < BS; ++i) {
-      float q = int8_round_div(a[i], s);
-      q = q > 127.0f ? 127.0f : q;
-      const float d = __fsub_rn(a[i], __fmul_rn(q, s));
-      d2[i] = __fmul_rn(d, d);
-    }
   }
   return sum8<BS>(d2);
 }
