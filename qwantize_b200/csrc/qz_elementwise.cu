@@ -315,30 +315,6 @@ __global__ void __launch_bounds__(256) spd_block_inverse_kernel(float* V, float*
     }
 }
 
-// dst = sign * src (transposed when trans != 0) for a rows x cols block of src,
-// with dst's split.  32 x 32 tiles through shared memory.
-__global__ void spd_copy_kernel(const float* __restrict__ src, float* dst, float* dst_s, int64_t ld, int64_t lo,
-                                int rows, int cols, float sign, int trans) {
-  __shared__ float t[32][33];
-  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // tile origin in src (col, row)
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int r = by + k, c = bx + threadIdx.x;
-    if (r < rows && c < cols) t[k][threadIdx.x] = src[(int64_t)r * ld + c];
-  }
-  __syncthreads();
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    int r, c;
-    float v;
-    if (trans) { r = bx + k; c = by + threadIdx.x; v = (r < cols && c < rows) ? t[threadIdx.x][k] : 0.0f;
-                 if (!(r < cols && c < rows)) continue; }
-    else { r = by + k; c = bx + threadIdx.x; if (!(r < rows && c < cols)) continue; v = t[k][threadIdx.x]; }
-    const int64_t i = (int64_t)r * ld + c;
-    const float o = sign < 0.0f ? -v : v;
-    dst[i] = o;
-    store_split(dst_s, i, lo, o);
-  }
-}
-
 cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st) {
   const int smem = 128 * 129 * 4;
   cudaError_t e = cudaFuncSetAttribute(spd_block_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -347,11 +323,5 @@ cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo,
   return cudaGetLastError();
 }
 
-cudaError_t launch_spd_copy(const float* src, float* dst, float* dst_s, int64_t ld, int64_t lo, int rows, int cols,
-                            float sign, int trans, cudaStream_t st) {
-  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)), block(32, 8);
-  spd_copy_kernel<<<grid, block, 0, st>>>(src, dst, dst_s, ld, lo, rows, cols, sign, trans);
-  return cudaGetLastError();
-}
 
 }  // namespace qz

@@ -95,6 +95,10 @@ struct GemmParams {
   float* Cs;
   float alpha;
   int beta;
+  // kTf3 extra copies of the result: D1 = d1_sign * C at the same position,
+  // D2 = d2_sign * C^T (value and split each, same leading dimension)
+  float *D1, *D1s, *D2, *D2s;
+  float d1_sign, d2_sign;
 };
 
 // ---------------------------------------------------------------------------
@@ -476,22 +480,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) cp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-          if (p.Cs) {
-            float hi[16], lo[16];
+          float hi[16], lo[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              uint32_t h, l;
-              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(o[q]));
-              hi[q] = __uint_as_float(h);
-              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(o[q] - hi[q]));
-              lo[q] = __uint_as_float(l);
-            }
+          for (int q = 0; q < 16; ++q) {  // tf32 split (round to nearest; odd: split(-v) = -split(v))
+            uint32_t h, l;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(o[q]));
+            hi[q] = __uint_as_float(h);
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(o[q] - hi[q]));
+            lo[q] = __uint_as_float(l);
+          }
+          if (p.Cs) {
             float4* hp = reinterpret_cast<float4*>(p.Cs + r * p.ldc + c0);
             float4* lp = reinterpret_cast<float4*>(p.Cs + p.cs_lo + r * p.ldc + c0);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               hp[q] = make_float4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
               lp[q] = make_float4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
+            }
+          }
+          if (p.D1) {
+            const float g = p.d1_sign;
+            float4* vp = reinterpret_cast<float4*>(p.D1 + r * p.ldc + c0);
+            float4* hp = reinterpret_cast<float4*>(p.D1s + r * p.ldc + c0);
+            float4* lp = reinterpret_cast<float4*>(p.D1s + p.cs_lo + r * p.ldc + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              vp[q] = make_float4(g * o[4 * q], g * o[4 * q + 1], g * o[4 * q + 2], g * o[4 * q + 3]);
+              hp[q] = make_float4(g * hi[4 * q], g * hi[4 * q + 1], g * hi[4 * q + 2], g * hi[4 * q + 3]);
+              lp[q] = make_float4(g * lo[4 * q], g * lo[4 * q + 1], g * lo[4 * q + 2], g * lo[4 * q + 3]);
+            }
+          }
+          if (p.D2) {  // transposed: lanes (consecutive rows r) write consecutive addresses
+            const float g = p.d2_sign;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const int64_t ti = (c0 + q) * p.ldc + r;
+              p.D2[ti] = g * o[q];
+              p.D2s[ti] = g * hi[q];
+              p.D2s[ti + p.cs_lo] = g * lo[q];
             }
           }
         }
@@ -689,8 +715,15 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   int sms = 0;
   int s = current_sms(&sms);
   if (s != QZ_OK) return s;
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<MODE>::kSmem);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute");
+  static bool attr_set[64] = {false};  // per device (a benign race: every thread sets the same value)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<MODE>::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
   const int64_t grid = p.n_tiles < sms ? p.n_tiles : sms;
   if (grid <= 0) return QZ_OK;
   gemm_kernel<MODE><<<(unsigned)grid, kGemmThreads, Geo<MODE>::kSmem, st>>>(a, b, c, p);
@@ -999,8 +1032,11 @@ struct SpdWork {
 // [ax, ax + k) of the split buffer behind map_a; B^T = rows [by, by + nn),
 // columns [bx, bx + k) of the split buffer behind map_b.
 static int tf3_gemm(const SpdWork& w, const CUtensorMap& ma, int ax, int ay, const CUtensorMap& mb, int bx, int by,
-                    int64_t m, int64_t nn, int64_t k, float* C, float* Cs, float alpha, int beta) {
+                    int64_t m, int64_t nn, int64_t k, float* C, float* Cs, float alpha, int beta,
+                    const GemmParams& extra) {
   GemmParams p{};
+  p.D1 = extra.D1; p.D1s = extra.D1s; p.d1_sign = extra.d1_sign;
+  p.D2 = extra.D2; p.D2s = extra.D2s; p.d2_sign = extra.d2_sign;
   p.M = m; p.N = nn; p.gk = k; p.K = w.n;
   p.a_x0 = ax; p.a_y0 = ay; p.a_lo_dx = 0; p.a_lo_dy = (int)w.n;
   p.b_x0 = bx; p.b_y0 = by; p.b_lo_dx = 0; p.b_lo_dy = (int)w.n;
@@ -1023,31 +1059,27 @@ static int spd_inverse_rec(const SpdWork& w, int64_t off, int64_t s) {
   const int64_t p12 = off * n + o2, p21 = o2 * n + off;
   int r = spd_inverse_rec(w, off, s1);  // X11
   if (r != QZ_OK) return r;
-  // T = X11 A12  (B^T = A12^T = A21: rows o2.., columns off..)
-  r = tf3_gemm(w, w.mS, (int)off, (int)off, w.mS, (int)off, (int)o2, s1, s2, s1, w.T + p12, w.Ts + p12, 1.0f, 0);
-  if (r != QZ_OK) return r;
-  r = cuda_status(launch_spd_copy(w.T + p12, w.Tt + p21, w.Tts + p21, n, n * n, (int)s1, (int)s2, 1.0f, 1, w.st),
-                  "spd transpose");
+  // T = X11 A12  (B^T = A12^T = A21: rows o2.., columns off..); its epilogue
+  // also writes T^T
+  GemmParams e{};
+  e.D2 = w.Tt + p21; e.D2s = w.Tts + p21; e.d2_sign = 1.0f;
+  r = tf3_gemm(w, w.mS, (int)off, (int)off, w.mS, (int)off, (int)o2, s1, s2, s1, w.T + p12, w.Ts + p12, 1.0f, 0, e);
   if (r != QZ_OK) return r;
   // S = A22 - T^T A12  (A = T^T: s2 x s1; B^T = A21)
   r = tf3_gemm(w, w.mTts, (int)off, (int)o2, w.mS, (int)off, (int)o2, s2, s2, s1, w.V + o2 * n + o2,
-               w.S + o2 * n + o2, -1.0f, 1);
+               w.S + o2 * n + o2, -1.0f, 1, GemmParams{});
   if (r != QZ_OK) return r;
   r = spd_inverse_rec(w, o2, s2);  // Y
   if (r != QZ_OK) return r;
-  // U = T Y  (B^T = Y, symmetric)
-  r = tf3_gemm(w, w.mTs, (int)o2, (int)off, w.mS, (int)o2, (int)o2, s1, s2, s2, w.U + p12, w.Us + p12, 1.0f, 0);
+  // U = T Y  (B^T = Y, symmetric); its epilogue also writes X12 = -U and X21 = -U^T
+  GemmParams u{};
+  u.D1 = w.V + p12; u.D1s = w.S + p12; u.d1_sign = -1.0f;
+  u.D2 = w.V + p21; u.D2s = w.S + p21; u.d2_sign = -1.0f;
+  r = tf3_gemm(w, w.mTs, (int)o2, (int)off, w.mS, (int)o2, (int)o2, s1, s2, s2, w.U + p12, w.Us + p12, 1.0f, 0, u);
   if (r != QZ_OK) return r;
   // X11 += U T^T  (B^T = T)
-  r = tf3_gemm(w, w.mUs, (int)o2, (int)off, w.mTs, (int)o2, (int)off, s1, s1, s2, w.V + off * n + off,
-               w.S + off * n + off, 1.0f, 1);
-  if (r != QZ_OK) return r;
-  // X12 = -U, X21 = -U^T
-  r = cuda_status(launch_spd_copy(w.U + p12, w.V + p12, w.S + p12, n, n * n, (int)s1, (int)s2, -1.0f, 0, w.st),
-                  "spd copy");
-  if (r != QZ_OK) return r;
-  return cuda_status(launch_spd_copy(w.U + p12, w.V + p21, w.S + p21, n, n * n, (int)s1, (int)s2, -1.0f, 1, w.st),
-                     "spd transpose");
+  return tf3_gemm(w, w.mUs, (int)o2, (int)off, w.mTs, (int)o2, (int)off, s1, s1, s2, w.V + off * n + off,
+                  w.S + off * n + off, 1.0f, 1, GemmParams{});
 }
 
 }  // namespace qz

@@ -67,8 +67,6 @@ cudaError_t launch_gptq_group(const GptqGroupArgs& a, int bs, int fmt, int metho
 cudaError_t launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, int num_sms, cudaStream_t st);
 
 cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st);
-cudaError_t launch_spd_copy(const float* src, float* dst, float* dst_s, int64_t ld, int64_t lo, int rows, int cols,
-                            float sign, int trans, cudaStream_t st);
 
 cudaError_t launch_quantize_grouped(const GroupArgs& g, int dtype, int bs, int fmt, int method, int num_sms,
                                     cudaStream_t st);
