@@ -705,9 +705,19 @@ def extras(ws, rank, device, peak_tf, args):
 def profile_call(spec):
     """Three launches of one quantization of the config-1 weight (native
     outputs), for ncu captures of a single kernel: spec "fmt,bs,method", e.g.
-    "nvfp4,16,optimal" or "int8,32,optimal"."""
+    "nvfp4,16,optimal" or "int8,32,optimal"; "gram" runs three full Grams of
+    65,536 tokens, "gptq" one GPTQ of the config weight."""
     from qwantize_b200 import _lib
     from qwantize_b200.synthetic import make_weight_device
+    if spec == "gram":  # three full Grams of 65,536 config-2 tokens (X 1.27 GB)
+        from qwantize_b200.hessian import gram
+        from qwantize_b200.synthetic import make_activations
+        dev = torch.device("cuda", 0)
+        X = make_activations(65536, K, seed=1, device=dev)
+        for _ in range(3):
+            gram(X, "full")
+        torch.cuda.synchronize(dev)
+        return
     if spec == "gptq":  # one GPTQ run: NVFP4 bs16 SSE-optimal, H from 65,536 tokens
         from qwantize_b200.gptq import gptq
         from qwantize_b200.hessian import gram
@@ -753,7 +763,7 @@ def main():
                     help="tokens for config 4's full 28672^2 Gram (0 skips it)")
     ap.add_argument("--profile-call", default=None,
                     help='only launch one quantization three times (ncu captures), e.g. "int8,32,optimal"; '
-                         '"gptq" runs one GPTQ of the config weight')
+                         '"gram" three full Grams of 65,536 tokens, "gptq" one GPTQ of the config weight')
     args = ap.parse_args()
     if args.profile_call:
         profile_call(args.profile_call)

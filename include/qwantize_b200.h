@@ -197,7 +197,7 @@ QZ_API int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int block_
  * allocates a small per-call counter buffer (cudaMallocAsync); this entry point
  * keeps those counters in a fixed 256 KB device array inside the library
  * instead, so it calls no allocator at all.  No counterpart in the reference.
- *   - Limit: at most 65,536 output tiles of 128 x 256, i.e. K <= 65280; larger
+ *   - Limit: at most 65,536 output tiles of 256 x 256, i.e. K <= 92416; larger
  *     K is rejected with QZ_ERR_INVALID before any device work.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.

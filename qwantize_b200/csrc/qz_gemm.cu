@@ -13,18 +13,23 @@
 //             squared-difference reduction done from TMEM in the epilogue, the
 //             T x M products never written.
 //
-// Kernel structure (one persistent CTA per SM, 192 threads):
-//   warp 0   TMA producer: a 4-stage ring of 48 KB operand stages
+// Kernel structure (one persistent CTA per SM, 192 threads; full Gram 320):
+//   warp 0   TMA producer: a ring of operand stages (4 x 48 KB; full Gram
+//            3 x 64 KB)
 //   warp 1   TMEM allocator + MMA issuer (one thread issues tcgen05.mma,
 //            tcgen05.commit frees a smem stage / publishes an accumulator)
 //   warps 2-5 epilogue: tcgen05.ld of the 128 x 256 fp32 accumulator
 //   Two accumulators (2 x 256 TMEM columns) let the epilogue of one tile overlap
-//   the main loop of the next.  Every mbarrier wait is bounded (2 s): on timeout
+//   the main loop of the next.  The full Gram's 256 x 256 tile uses both as one
+//   (rows 0-127 and 128-255) and drains them with 8 epilogue warps (2-9); its
+//   units are long (up to 4096 K-steps), so the unoverlapped epilogue costs
+//   about 1%.  Every mbarrier wait is bounded (2 s): on timeout
 //   the kernel records an error flag, all roles stop, TMEM is freed, and the
 //   host reports QZ_ERR_TIMEOUT.  No TMA multicast anywhere.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -39,7 +44,6 @@ int fail(int code, const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
 int current_sms(int* sms);
 
-constexpr int kGemmThreads = 192;
 constexpr int kBM = 128, kBK = 64;  // tile rows, K-step (64 bf16 = one 128-byte swizzle row)
 
 enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3, kTf3 = 4 };
@@ -49,20 +53,31 @@ enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3, kTf3 = 4 
 // symmetric-positive-definite inverse).
 __host__ __device__ constexpr bool tf_mode(int mode) { return mode == kGptq || mode == kTf3; }
 
-// Per-mode geometry.  Full Gram / metrics: 128 x 256 tiles, A 16 KB + B 32 KB
-// per stage, 4 stages, two 256-column accumulators (all 512 TMEM columns).
+// Per-mode geometry.  Full Gram: 256 x 256 tiles, A 32 KB + B 32 KB per stage
+// (a diagonal tile loads one panel for both), 3 stages; each stage feeds two
+// M = 128 MMAs that share the B panel, so a stage is 1024 tensor cycles for 64
+// KB of operands (two thirds of the L2 -> shared traffic per flop of a 128 x
+// 256 tile).  Metrics: 128 x 256 tiles, A 16 KB + B 32 KB per stage, 4 stages,
+// two 256-column accumulators (all 512 TMEM columns).
 // Block-diagonal Gram: 128 x 128 diagonal tiles whose A and B panels are the
 // same columns of X, so one 16 KB panel per stage feeds both operands; 8 stages.
 // GPTQ update: 128 x 128 tiles of fp32 operands as tf32 high / low pairs; a
 // stage holds 32 columns of K (128 bytes per row) of A_hi, A_lo, B_hi, B_lo.
 template <int MODE>
 struct Geo {
+  static constexpr int BM = MODE == kGramFull ? 256 : kBM;  // output tile rows
   static constexpr int BN = (MODE == kGramDiag || tf_mode(MODE)) ? 128 : 256;
-  static constexpr int kABytes = tf_mode(MODE) ? 2 * kBM * 128 : kBM * kBK * 2;
+  static constexpr int kABytes = tf_mode(MODE) ? 2 * kBM * 128 : BM * kBK * 2;
   static constexpr int kBBytes = MODE == kGramDiag ? 0 : (tf_mode(MODE) ? 2 * BN * 128 : BN * kBK * 2);
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = MODE == kGramDiag ? 8 : (tf_mode(MODE) ? 3 : 4);
+  static constexpr int kStages = MODE == kGramDiag ? 8 : ((tf_mode(MODE) || MODE == kGramFull) ? 3 : 4);
   static constexpr int kTmemCols = 2 * BN;
+  // Full Gram: one 256 x 256 tile is two M = 128 accumulators (all 512 TMEM
+  // columns, no double buffer) drained by 8 epilogue warps; other modes keep
+  // two accumulators, 4 epilogue warps
+  static constexpr int kAccs = MODE == kGramFull ? 1 : 2;
+  static constexpr int kEpiThreads = MODE == kGramFull ? 256 : 128;
+  static constexpr int kThreads = 64 + kEpiThreads;
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -75,6 +90,11 @@ struct GemmParams {
   int64_t seg_rows, band;      // kGramFull: token rows per segment, tile rows per band
   int* seq;                    // kGramFull: per-tile count of segments already added
   int64_t tiles_per_seg;       // kGramFull: tiles in one segment (units = tiles x segments)
+  // kGramFull, last wave: units from tail_start on are the last tail_tiles
+  // tiles of the last segment (first tile tail_tile0, rows from tail_r0), each
+  // cut into pieces of tail_piece_rows token rows that count as further
+  // segments (last_seg, last_seg + 1, ...) of their tile
+  int64_t tail_start, tail_tiles, tail_tile0, tail_r0, tail_piece_rows, last_seg;
   float* H;
   float* partials;      // kGramDiag: splits-1 partial (K/bs, bs, bs) buffers
   double* sums;
@@ -204,14 +224,14 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int mode, int64
     nj = t % p.tiles_n;
     return;
   }
-  // kGramFull: tiles (mi, nj) with nj*256 + 255 >= mi*128, enumerated in bands
-  // of p.band tile rows, column by column inside a band, so the ~148 tiles in
+  // kGramFull: 256 x 256 tiles (mi, nj) with nj >= mi, enumerated in bands of
+  // p.band tile rows, column by column inside a band, so the ~148 tiles in
   // flight share few column panels of X (L2 reuse).
   int64_t r = t;
   for (int64_t b0 = 0; b0 < p.tiles_m; b0 += p.band) {
     const int64_t rows_end = b0 + p.band < p.tiles_m ? b0 + p.band : p.tiles_m;
-    for (int64_t n = (b0 * kBM) / 256; n < p.tiles_n; ++n) {
-      const int64_t hi = rows_end < 2 * n + 2 ? rows_end : 2 * n + 2;  // rows with mi/2 <= n
+    for (int64_t n = b0; n < p.tiles_n; ++n) {
+      const int64_t hi = rows_end < n + 1 ? rows_end : n + 1;  // rows with mi <= n
       const int64_t cnt = hi - b0;
       if (r < cnt) { mi = b0 + r; nj = n; return; }
       r -= cnt;
@@ -246,11 +266,20 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t t) {
   if (MODE == kGramDiag) {
     tile_coords(p, MODE, t, u.mi, u.nj);  // nj = split index
     u.r0 = u.nj * p.split_rows;
-  } else {
+  } else if (t < p.tail_start) {
     u.seg = t / p.tiles_per_seg;
     u.tile = t % p.tiles_per_seg;
     tile_coords(p, MODE, u.tile, u.mi, u.nj);
     u.r0 = u.seg * p.seg_rows;
+  } else {
+    const int64_t q = t - p.tail_start, piece = q / p.tail_tiles;
+    u.tile = p.tail_tile0 + q % p.tail_tiles;
+    u.seg = p.last_seg + piece;
+    tile_coords(p, MODE, u.tile, u.mi, u.nj);
+    u.r0 = p.tail_r0 + piece * p.tail_piece_rows;
+    const int64_t r1 = u.r0 + p.tail_piece_rows < p.T ? u.r0 + p.tail_piece_rows : p.T;
+    u.steps = (r1 - u.r0 + kBK - 1) / kBK;
+    return u;
   }
   const int64_t rows = MODE == kGramDiag ? p.split_rows : p.seg_rows;
   const int64_t r1 = u.r0 + rows < p.T ? u.r0 + rows : p.T;
@@ -259,7 +288,7 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t t) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(Geo<MODE>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_c, GemmParams p) {
   using G = Geo<MODE>;
@@ -273,12 +302,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done = tempty + 2;  // the MMA issuer's final commit (all its MMAs retired)
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_base_s + 1);
+  volatile int* go_s = abort_s + 1;  // full Gram: the segment-order verdict of this tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 128); }
+    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, G::kEpiThreads); }
     mbar_init(mma_done, 1);
     *abort_s = 0;
     fence_barrier_init();
@@ -315,7 +345,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!wait(empty + s, ((it / G::kStages) & 1) ^ 1, kDevErrLoadTimeout)) goto producer_done;
           unsigned char* sa = smem + s * G::kStageBytes;
           unsigned char* sb = sa + G::kABytes;
-          mbar_arrive_expect_tx(full + s, G::kStageBytes);
+          // a diagonal full-Gram tile reads one panel for both operands
+          const bool one_panel = MODE == kGramFull && mi == nj;
+          mbar_arrive_expect_tx(full + s, one_panel ? G::kABytes : G::kStageBytes);
           if (tf_mode(MODE)) {
             // high and low parts of a 128 x 32 tile of A and of B^T (K-major)
             const int kx = (int)(ks * 32), ay = p.a_y0 + (int)(mi * kBM), by = p.b_y0 + (int)(nj * 128);
@@ -330,10 +362,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_load_2d(sb + 128 * kBK * 2, &map_c, kx, (int)(nj * 128), full + s);  // W_dq rows
           } else {
             const int ty = (int)(r0 + ks * kBK);
-            const int i0 = (int)(mi * kBM);
-            tma_load_2d(sa, &map_a, i0, ty, full + s);
-            tma_load_2d(sa + 8192, &map_a, i0 + 64, ty, full + s);
-            if (MODE == kGramFull) {
+            const int i0 = (int)(mi * G::BM);
+#pragma unroll
+            for (int q = 0; q < G::BM / 64; ++q) tma_load_2d(sa + 8192 * q, &map_a, i0 + 64 * q, ty, full + s);
+            if (MODE == kGramFull && !one_panel) {
               const int j0 = (int)(nj * BN);
 #pragma unroll
               for (int q = 0; q < 4; ++q) tma_load_2d(sb + 8192 * q, &map_a, j0 + 64 * q, ty, full + s);
@@ -356,9 +388,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t idesc = tf_mode(MODE) ? instr_desc_tf32(kBM, BN) : instr_desc(kBM, BN, mn, mn);
       uint32_t it = 0, lt = 0;
       for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
-        const int64_t k_steps = unit_of<MODE>(p, t).steps;
-        const uint32_t acc = lt & 1;
-        if (!wait(tempty + acc, ((lt >> 1) & 1) ^ 1, kDevErrMmaTimeout)) break;
+        const Unit u = unit_of<MODE>(p, t);
+        const int64_t k_steps = u.steps;
+        const uint32_t acc = G::kAccs == 2 ? (lt & 1) : 0u;
+        const uint32_t phase = G::kAccs == 2 ? ((lt >> 1) & 1) : (lt & 1);
+        if (!wait(tempty + acc, phase ^ 1, kDevErrMmaTimeout)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
@@ -367,7 +401,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!wait(full + s, (it / G::kStages) & 1, kDevErrMmaTimeout)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * G::kStageBytes);
-          const uint32_t sb = MODE == kGramDiag ? sa : sa + G::kABytes;
+          const uint32_t sb = (MODE == kGramDiag || (MODE == kGramFull && u.mi == u.nj)) ? sa : sa + G::kABytes;
           if constexpr (tf_mode(MODE)) {
             // D += A_hi B_hi + A_hi B_lo + A_lo B_hi, 8 tf32 (32 bytes) of K per MMA
 #pragma unroll
@@ -377,6 +411,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               umma_tf32(d_tmem, al, bh, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
               umma_tf32(d_tmem, ah, bl, idesc, 1u);
               umma_tf32(d_tmem, ah, bh, idesc, 1u);
+            }
+          } else if constexpr (MODE == kGramFull) {
+            // rows 0-127 and 128-255 of the tile against the same 256 columns
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t bd = smem_desc(sb + kk * 2048, p.lbo, p.sbo);
+              const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+              umma_bf16(d_tmem, smem_desc(sa + kk * 2048, p.lbo, p.sbo), bd, idesc, accum);
+              umma_bf16(d_tmem + BN, smem_desc(sa + 16384 + kk * 2048, p.lbo, p.sbo), bd, idesc, accum);
             }
           } else {
 #pragma unroll
@@ -402,18 +445,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait_bounded(mma_done, 0u, kDevErrMmaTimeout);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..5, full Gram 2..9) ----------------
     const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;     // accumulator row of this thread
+    const int half = (warp - 2) >> 2;        // full Gram: which M = 128 accumulator
     uint32_t lt = 0;
     double part0 = 0.0, part1 = 0.0;
     for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
       const Unit u = unit_of<MODE>(p, t);
       const int64_t mi = u.mi, nj = u.nj;
-      const uint32_t acc = lt & 1;
-      if (!wait(tfull + acc, (lt >> 1) & 1, kDevErrEpilogueTimeout)) break;
+      const uint32_t acc = G::kAccs == 2 ? (lt & 1) : 0u;
+      const uint32_t phase = G::kAccs == 2 ? ((lt >> 1) & 1) : (lt & 1);
+      if (!wait(tfull + acc, phase, kDevErrEpilogueTimeout)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const uint32_t taddr =
+          tmem_base + ((uint32_t)(quarter * 32) << 16) + (MODE == kGramFull ? half : acc) * BN;
       if (MODE == kMetrics) {
         const int64_t trow = mi * kBM + row;
         float e = 0.0f, r2 = 0.0f;
@@ -572,10 +618,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
-        // segments of one tile are added in order: wait until the previous
-        // segment of this tile has been written (bounded), add, then publish
+        // segments of one tile are added in order: one thread waits until the
+        // previous segment of this tile has been written (bounded) and hands
+        // its verdict to all epilogue warps through shared memory, so they
+        // all continue or all stop; add, then publish
         bool go = true;
-        if (lane == 0) {
+        if (warp == 2 && lane == 0) {
           const volatile int* sq = p.seq + u.tile;
           if (*sq < u.seg) {
             const uint64_t t0 = globaltimer_ns();
@@ -590,12 +638,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               __nanosleep(256);
             }
           }
+          *go_s = go ? 1 : 0;
         }
-        go = __shfl_sync(0xffffffffu, go, 0);
+        asm volatile("bar.sync 1, %0;" ::"n"(G::kEpiThreads) : "memory");
+        go = *go_s != 0;
         if (!go) break;
         __threadfence();
         const bool add = u.seg > 0 || p.accumulate;
-        const int64_t i = mi * kBM + row;
+        const int64_t i = mi * G::BM + half * 128 + row;
         const int64_t j0 = nj * BN;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
@@ -633,7 +683,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (MODE == kGramFull) {
         __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+        asm volatile("bar.sync 1, %0;" ::"n"(G::kEpiThreads) : "memory");  // the epilogue warps
         if (warp == 2 && lane == 0) atomicExch(p.seq + u.tile, (int)(u.seg + 1));
       }
       tc_fence_before();
@@ -726,13 +776,14 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   }
   const int64_t grid = p.n_tiles < sms ? p.n_tiles : sms;
   if (grid <= 0) return QZ_OK;
-  gemm_kernel<MODE><<<(unsigned)grid, kGemmThreads, Geo<MODE>::kSmem, st>>>(a, b, c, p);
+  gemm_kernel<MODE><<<(unsigned)grid, Geo<MODE>::kThreads, Geo<MODE>::kSmem, st>>>(a, b, c, p);
   return cuda_status(cudaGetLastError(), "gemm launch");
 }
 
 
-// Full Gram: token rows per segment (a multiple of 64) and tile rows per band.
-constexpr int64_t kGramSegmentRows = 262144;
+// Full Gram: token rows per segment (a multiple of 64), the cost of one unit's
+// epilogue in rows of its main loop, and tile rows per band.
+constexpr int64_t kGramSegmentRows = 262144, kGramEpilogueRows = 1024;
 constexpr int64_t kGramBand = 4;
 // MN-major descriptor offsets: 8 KB between 64-element swizzle atoms along M / N,
 // 1 KB between 8-row groups along K.
@@ -792,6 +843,47 @@ cudaError_t read_device_error_gemm(unsigned* out, bool clear) {
   return cudaMemcpyToSymbol(qz_device_error, &zero, sizeof(unsigned));
 }
 
+// Full Gram geometry: 256 x 256 tiles on and above the diagonal, per segment.
+static int64_t full_gram_tiles(int64_t K) {
+  const int64_t t = (K + 255) / 256;
+  return t * (t + 1) / 2;
+}
+
+// Units run segment-major, one (tile, segment) unit per CTA at a time, so when
+// the unit count leaves a partial last wave of r units (r <= tiles), those
+// units -- the last r tiles of the last segment -- are cut into m row pieces
+// each and the r*m pieces share the wave's idle SMs.  The pieces of a tile add
+// into H in order (further segments of that tile), so the result stays
+// deterministic; the order costs m epilogues in a row, so m balances the
+// piece length against m epilogues (about kGramEpilogueRows rows each).
+static void full_gram_params(GemmParams& p, int64_t T, int64_t K, int sms) {
+  p.tiles_m = p.tiles_n = (K + 255) / 256;
+  const int64_t n = full_gram_tiles(K);
+  p.tiles_per_seg = n;
+  p.seg_rows = kGramSegmentRows;
+  const int64_t segs = (T + p.seg_rows - 1) / p.seg_rows;
+  p.n_tiles = n * segs;
+  p.band = kGramBand;
+  p.tail_start = p.n_tiles;
+  p.tail_tiles = 1;
+  const int64_t r = p.n_tiles % sms;
+  if (r == 0 || r > n || sms < 2) return;
+  const int64_t last_r0 = (segs - 1) * p.seg_rows, last_rows = T - last_r0;
+  int64_t m = (int64_t)(sqrt((double)last_rows / kGramEpilogueRows) + 0.5);
+  if (m > sms / r) m = sms / r;
+  if (m < 2) return;
+  int64_t piece = ((last_rows + m - 1) / m + kBK - 1) / kBK * kBK;
+  m = (last_rows + piece - 1) / piece;  // every piece non-empty
+  if (m < 2) return;
+  p.tail_start = p.n_tiles - r;
+  p.tail_tiles = r;
+  p.tail_tile0 = n - r;
+  p.tail_r0 = last_r0;
+  p.tail_piece_rows = piece;
+  p.last_seg = segs - 1;
+  p.n_tiles = p.tail_start + r * m;
+}
+
 }  // namespace qz
 
 using namespace qz;
@@ -827,14 +919,8 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
     // sweep the same token rows at about the same time, so the column panels
     // they share stay in L2.  A tile's segments are added in segment order
     // (per-tile counters in scratch), so H is deterministic and exactly symmetric.
-    p.tiles_n = (K + 255) / 256;
-    int64_t n = 0;
-    for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
-    p.tiles_per_seg = n;
-    p.seg_rows = kGramSegmentRows;
-    const int64_t n_segs = (T + p.seg_rows - 1) / p.seg_rows;
-    p.n_tiles = n * n_segs;
-    p.band = kGramBand;
+    full_gram_params(p, T, K, sms);
+    const int64_t n = p.tiles_per_seg;
     p.T = T;
     p.accumulate = accumulate;
     CUtensorMap map;
@@ -914,14 +1000,11 @@ extern "C" int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int
   if (K > 2147483647LL || T > 2147483647LL) return fail(QZ_ERR_INVALID, "T and K must fit in int32");
   if (!H) return fail(QZ_ERR_INVALID, "H is NULL");
   GemmParams p{};
-  p.tiles_m = (K + kBM - 1) / kBM;
-  p.tiles_n = (K + 255) / 256;
-  int64_t n = 0;
-  for (int64_t mi = 0; mi < p.tiles_m; ++mi) n += p.tiles_n - (mi * kBM) / 256;
+  const int64_t n = full_gram_tiles(K);
   if (n > kNoAllocMaxTiles)
     return fail(QZ_ERR_INVALID,
                 "qz_gram_full_noalloc: K = %lld needs %lld output tiles; the fixed scratch holds %lld "
-                "(K <= 65280); use qz_gram",
+                "(K <= 92416); use qz_gram",
                 (long long)K, (long long)n, (long long)kNoAllocMaxTiles);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (T == 0) {
@@ -939,10 +1022,10 @@ extern "C" int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int
   p.K = K; p.M = 0; p.bs = 16; p.H = H; p.T = T; p.accumulate = accumulate;
   p.lbo = kMnLbo;
   p.sbo = kMnSbo;
-  p.tiles_per_seg = n;
-  p.seg_rows = kGramSegmentRows;
-  p.n_tiles = n * ((T + p.seg_rows - 1) / p.seg_rows);
-  p.band = kGramBand;
+  int sms = 0;
+  s = current_sms(&sms);
+  if (s != QZ_OK) return s;
+  full_gram_params(p, T, K, sms);
   p.seq = counters;
   CUtensorMap map;
   s = make_map(&map, X, (uint64_t)K, (uint64_t)T, 64, 64);

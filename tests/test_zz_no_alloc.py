@@ -51,6 +51,6 @@ def test_noalloc_gram_matches_qz_gram_twice():
 def test_noalloc_gram_rejects_too_large_k():
     from qwantize_b200 import _lib
     L = _lib.load()
-    st = L.qz_gram_full_noalloc(ctypes.c_void_p(16), 64, 65288, 0, ctypes.c_void_p(16), None)
+    st = L.qz_gram_full_noalloc(ctypes.c_void_p(16), 64, 92424, 0, ctypes.c_void_p(16), None)
     assert st == _lib.QZ_ERR_INVALID
-    assert b"65280" in L.qz_last_error()
+    assert b"92416" in L.qz_last_error()
