@@ -600,7 +600,7 @@ def extras(ws, rank, device, peak_tf, args):
     ms_admm = _ev_time(lambda: admm_fp32(Wb, -1, False, Hb, Hn, Minv), stream, 3)
     H = torch.empty(Kx, Kx, device=device)
     _barrier(ws)
-    ms_full = _max_over_ranks(_ev_time(lambda: gram(X, "full", out=H), stream), ws, device)
+    ms_full = _max_over_ranks(_ev_time(lambda: gram(X, "full", out=H), stream, 3), ws, device)
     ar_ms = None
     if ws > 1:
         _barrier(ws)
@@ -674,7 +674,7 @@ def extras(ws, rank, device, peak_tf, args):
         X4 = make_activations(a1 - a0, K4, seed=4, device=device, t0=a0)
         H4 = torch.empty(K4, K4, device=device)
         _barrier(ws)
-        ms_g4 = _max_over_ranks(_ev_time(lambda: gram(X4, "full", out=H4), stream), ws, device)
+        ms_g4 = _max_over_ranks(_ev_time(lambda: gram(X4, "full", out=H4), stream, 2), ws, device)
         ar4 = None
         if ws > 1:
             _barrier(ws)

@@ -13,18 +13,20 @@
 //             squared-difference reduction done from TMEM in the epilogue, the
 //             T x M products never written.
 //
-// Kernel structure (one persistent CTA per SM, 192 threads; full Gram 320):
-//   warp 0   TMA producer: a ring of operand stages (4 x 48 KB; full Gram
-//            3 x 64 KB)
+// Kernel structure (one persistent CTA per SM, 192 threads; full Gram and
+// metrics 320):
+//   warp 0   TMA producer: a ring of operand stages (4 x 48 KB; full Gram and
+//            metrics 3 x 64 KB)
 //   warp 1   TMEM allocator + MMA issuer (one thread issues tcgen05.mma,
 //            tcgen05.commit frees a smem stage / publishes an accumulator)
-//   warps 2-5 epilogue: tcgen05.ld of the 128 x 256 fp32 accumulator
+//   warps 2-5 epilogue: tcgen05.ld of the 128 x N fp32 accumulator
 //   Two accumulators (2 x 256 TMEM columns) let the epilogue of one tile overlap
-//   the main loop of the next.  The full Gram's 256 x 256 tile uses both as one
-//   (rows 0-127 and 128-255) and drains them with 8 epilogue warps (2-9); its
-//   units are long (up to 4096 K-steps), so the unoverlapped epilogue costs
-//   about 1%.  Every mbarrier wait is bounded (2 s): on timeout
-//   the kernel records an error flag, all roles stop, TMEM is freed, and the
+//   the main loop of the next.  The 256-row tiles of the full Gram and the
+//   metrics use both as one (rows 0-127 and 128-255) and drain them with 8
+//   epilogue warps (2-9); their units are long (hundreds to thousands of
+//   K-steps), so the unoverlapped epilogue costs 1-2%.  Every mbarrier wait is
+//   bounded (2 s): on timeout the kernel records an error flag, all roles stop,
+//   TMEM is freed, and the
 //   host reports QZ_ERR_TIMEOUT.  No TMA multicast anywhere.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -52,31 +54,33 @@ enum GemmMode { kGramFull = 0, kGramDiag = 1, kMetrics = 2, kGptq = 3, kTf3 = 4 
 // pairs (kGptq: GPTQ's error update; kTf3: C = beta C + alpha A B for the
 // symmetric-positive-definite inverse).
 __host__ __device__ constexpr bool tf_mode(int mode) { return mode == kGptq || mode == kTf3; }
+// The modes whose 256-row output tile is two M = 128 MMAs sharing one B panel.
+__host__ __device__ constexpr bool wide_mode(int mode) { return mode == kGramFull || mode == kMetrics; }
 
 // Per-mode geometry.  Full Gram: 256 x 256 tiles, A 32 KB + B 32 KB per stage
 // (a diagonal tile loads one panel for both), 3 stages; each stage feeds two
 // M = 128 MMAs that share the B panel, so a stage is 1024 tensor cycles for 64
 // KB of operands (two thirds of the L2 -> shared traffic per flop of a 128 x
-// 256 tile).  Metrics: 128 x 256 tiles, A 16 KB + B 32 KB per stage, 4 stages,
-// two 256-column accumulators (all 512 TMEM columns).
+// 256 tile).  Metrics: likewise 256 token rows x [128 rows of W; 128 of W_dq],
+// A 32 KB + B 32 KB per stage, 3 stages.
 // Block-diagonal Gram: 128 x 128 diagonal tiles whose A and B panels are the
 // same columns of X, so one 16 KB panel per stage feeds both operands; 8 stages.
 // GPTQ update: 128 x 128 tiles of fp32 operands as tf32 high / low pairs; a
 // stage holds 32 columns of K (128 bytes per row) of A_hi, A_lo, B_hi, B_lo.
 template <int MODE>
 struct Geo {
-  static constexpr int BM = MODE == kGramFull ? 256 : kBM;  // output tile rows
+  static constexpr int BM = wide_mode(MODE) ? 256 : kBM;  // output tile rows
   static constexpr int BN = (MODE == kGramDiag || tf_mode(MODE)) ? 128 : 256;
   static constexpr int kABytes = tf_mode(MODE) ? 2 * kBM * 128 : BM * kBK * 2;
   static constexpr int kBBytes = MODE == kGramDiag ? 0 : (tf_mode(MODE) ? 2 * BN * 128 : BN * kBK * 2);
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = MODE == kGramDiag ? 8 : ((tf_mode(MODE) || MODE == kGramFull) ? 3 : 4);
+  static constexpr int kStages = MODE == kGramDiag ? 8 : ((tf_mode(MODE) || wide_mode(MODE)) ? 3 : 4);
   static constexpr int kTmemCols = 2 * BN;
   // Full Gram: one 256 x 256 tile is two M = 128 accumulators (all 512 TMEM
   // columns, no double buffer) drained by 8 epilogue warps; other modes keep
   // two accumulators, 4 epilogue warps
-  static constexpr int kAccs = MODE == kGramFull ? 1 : 2;
-  static constexpr int kEpiThreads = MODE == kGramFull ? 256 : 128;
+  static constexpr int kAccs = wide_mode(MODE) ? 1 : 2;
+  static constexpr int kEpiThreads = wide_mode(MODE) ? 256 : 128;
   static constexpr int kThreads = 64 + kEpiThreads;
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(Geo<MODE>::kThreads, 1)
             tma_load_2d(sb + 16384, &map_b, p.b_x0 + p.b_lo_dx + kx, by + p.b_lo_dy, full + s);
           } else if (MODE == kMetrics) {
             const int kx = (int)(ks * kBK);
-            tma_load_2d(sa, &map_a, kx, (int)(mi * kBM), full + s);                 // X rows (t)
+            tma_load_2d(sa, &map_a, kx, (int)(mi * G::BM), full + s);               // X rows (t)
             tma_load_2d(sb, &map_b, kx, (int)(nj * 128), full + s);                 // W rows
             tma_load_2d(sb + 128 * kBK * 2, &map_c, kx, (int)(nj * 128), full + s);  // W_dq rows
           } else {
@@ -412,6 +416,16 @@ __global__ void __launch_bounds__(Geo<MODE>::kThreads, 1)
               umma_tf32(d_tmem, ah, bl, idesc, 1u);
               umma_tf32(d_tmem, ah, bh, idesc, 1u);
             }
+          } else if constexpr (MODE == kMetrics) {
+            // X rows 0-127 and 128-255 of the tile against the same [W; W_dq]
+            // panel (K-major: row 128 starts 16 KB into the A panel)
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t bd = smem_desc(sb + kk * 32, 16, 1024);
+              const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+              umma_bf16(d_tmem, smem_desc(sa + kk * 32, 16, 1024), bd, idesc, accum);
+              umma_bf16(d_tmem + BN, smem_desc(sa + 16384 + kk * 32, 16, 1024), bd, idesc, accum);
+            }
           } else if constexpr (MODE == kGramFull) {
             // rows 0-127 and 128-255 of the tile against the same 256 columns
 #pragma unroll
@@ -459,9 +473,9 @@ __global__ void __launch_bounds__(Geo<MODE>::kThreads, 1)
       if (!wait(tfull + acc, phase, kDevErrEpilogueTimeout)) break;
       tc_fence_after();
       const uint32_t taddr =
-          tmem_base + ((uint32_t)(quarter * 32) << 16) + (MODE == kGramFull ? half : acc) * BN;
+          tmem_base + ((uint32_t)(quarter * 32) << 16) + (wide_mode(MODE) ? half : acc) * BN;
       if (MODE == kMetrics) {
-        const int64_t trow = mi * kBM + row;
+        const int64_t trow = mi * G::BM + half * 128 + row;
         float e = 0.0f, r2 = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < 128; c += 16) {
@@ -981,13 +995,13 @@ extern "C" int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, con
     return fail(QZ_ERR_INVALID, "X, W and W_dq must be 16-byte aligned");
   if (T == 0) return QZ_OK;
   CUtensorMap mx, mw, mq;
-  int s = make_map(&mx, X, (uint64_t)K, (uint64_t)T, 64, 128);
+  int s = make_map(&mx, X, (uint64_t)K, (uint64_t)T, 64, 256);
   if (s == QZ_OK) s = make_map(&mw, W, (uint64_t)K, (uint64_t)M, 64, 128);
   if (s == QZ_OK) s = make_map(&mq, W_dq, (uint64_t)K, (uint64_t)M, 64, 128);
   if (s != QZ_OK) return s;
   GemmParams p{};
   p.T = T; p.K = K; p.M = M; p.sums = sums;
-  p.tiles_m = (T + kBM - 1) / kBM;
+  p.tiles_m = (T + Geo<kMetrics>::BM - 1) / Geo<kMetrics>::BM;
   p.tiles_n = (M + 127) / 128;
   p.n_tiles = p.tiles_m * p.tiles_n;
   return launch_gemm<kMetrics>(mx, mw, mq, p, static_cast<cudaStream_t>(stream));
