@@ -798,6 +798,8 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
 // Full Gram: token rows per segment (a multiple of 64), the cost of one unit's
 // epilogue in rows of its main loop, and tile rows per band.
 constexpr int64_t kGramSegmentRows = 262144, kGramEpilogueRows = 1024;
+// Block-diagonal Gram: a unit's fixed cost (pipeline fill, epilogue) in rows.
+constexpr int64_t kDiagUnitRows = 256;
 constexpr int64_t kGramBand = 4;
 // MN-major descriptor offsets: 8 KB between 64-element swizzle atoms along M / N,
 // 1 KB between 8-row groups along K.
@@ -957,10 +959,21 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   p.T = T;
   p.accumulate = accumulate;
   p.tiles_n = 1;
-  int64_t splits = (8 * (int64_t)sms + p.tiles_m - 1) / p.tiles_m;
-  const int64_t max_splits = (T + 4095) / 4096;  // keep >= 4096 rows per unit
-  splits = splits < max_splits ? splits : max_splits;
-  if (splits < 1) splits = 1;
+  // Token splits: every CTA runs whole (tile, split) units, so the count is
+  // chosen to minimise waves x (rows per unit + a unit's fixed cost in rows),
+  // with at least 4096 rows per unit (tiles x splits a multiple of the SM
+  // count fills every wave).
+  int64_t splits = 1;
+  {
+    const int64_t max_splits = T / 4096 < 1024 ? T / 4096 : 1024;
+    int64_t best = -1;
+    for (int64_t S = 1; S <= (max_splits > 1 ? max_splits : 1); ++S) {
+      const int64_t rows = ((T + S - 1) / S + kBK - 1) / kBK * kBK;
+      const int64_t units = p.tiles_m * ((T + rows - 1) / rows);
+      const int64_t cost = (units + sms - 1) / sms * (rows + kDiagUnitRows);
+      if (best < 0 || cost < best) { best = cost; splits = S; }
+    }
+  }
   p.split_rows = ((T + splits - 1) / splits + kBK - 1) / kBK * kBK;
   splits = (T + p.split_rows - 1) / p.split_rows;
   p.splits = splits;
