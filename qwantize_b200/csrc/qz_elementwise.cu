@@ -227,100 +227,137 @@ __device__ __forceinline__ void store_split(float* S, int64_t i, int64_t lo, flo
   S[i + lo] = __uint_as_float(l);
 }
 
-// In-place inverse of one s x s diagonal block (s <= 128, a multiple of 32)
-// by Gauss-Jordan elimination without pivoting, in double precision (a
+// In-place inverse of one s x s diagonal block (s <= 96, a multiple of 32)
+// by the symmetric Gauss-Jordan sweep without pivoting, in double precision (a
 // symmetric positive definite matrix needs no pivoting; a pivot <= 0 means the
-// input is not positive definite: *bad is set).  16 x 16 threads, each holding
-// an 8 x 8 set of elements (rows ty + 16a, columns tx + 16b) in registers;
-// per pivot only row p and column p pass through shared memory (two buffers,
-// so one barrier per pivot).
+// input is not positive definite: *bad is set).
+//
+// After the pivots of a set P are swept, the matrix is [A_PP^-1, A_PP^-1 A_PQ;
+// -A_QP A_PP^-1, Schur complement] (Q the rest): the P x P and Q x Q blocks are
+// symmetric and the P x Q block is minus the transpose of the Q x P block.  So
+// only the upper triangle is kept and updated, and the pivot's row and column
+// both come from its "cross" u (u[k] = U[p][k] for k >= p, U[k][p] for k < p):
+// column p is u, row p is u with the swept entries (k < p) negated.
+//
+// The block lives in a D x D frame (D = 64 or 96, the smallest >= s;
+// identity outside s) over 16 x 16 threads, each holding the (D/16)^2 elements
+// (rows ty + 16a, columns tx + 16b) in registers; per pivot only its cross
+// passes through shared memory (two buffers, so one barrier per pivot).
+// Double precision is slow on this part (a pivot costs about 1 us, mostly the
+// latency of its dependent double operations), so frames follow s, only the
+// upper triangle's elements are updated, and the recursion stops at 96.
+template <int D>
 __global__ void __launch_bounds__(256) spd_block_inverse_kernel(float* V, float* S, int64_t ld, int64_t lo, int s,
                                                                 int* bad) {
-  __shared__ double rowp[2][128], colp[2][128];
+  constexpr int E = D / 16;
+  __shared__ double cross[2][D];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  double A[8][8];
+  double A[E][E];
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
+  for (int a = 0; a < E; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) {
+    for (int b = 0; b < E; ++b) {
       const int i = ty + 16 * a, j = tx + 16 * b;
       A[a][b] = (i < s && j < s) ? (double)V[i * ld + j] : (i == j ? 1.0 : 0.0);
     }
   for (int p = 0; p < s; ++p) {
     const int buf = p & 1, pa = p >> 4, pr = p & 15;
-    if (ty == pr) {
+    if (ty == pr) {  // row p: the cross at k >= p
 #pragma unroll
-      for (int b = 0; b < 8; ++b) if (b * 16 + tx < 128) {
+      for (int b = 0; b < E; ++b) {
         double v = 0.0;
 #pragma unroll
-        for (int a = 0; a < 8; ++a) v = a == pa ? A[a][b] : v;
-        rowp[buf][tx + 16 * b] = v;
+        for (int a = 0; a < E; ++a) v = a == pa ? A[a][b] : v;
+        if (tx + 16 * b >= p) cross[buf][tx + 16 * b] = v;
       }
     }
-    if (tx == pr) {
+    if (tx == pr) {  // column p: the cross at k < p
 #pragma unroll
-      for (int a = 0; a < 8; ++a) {
+      for (int a = 0; a < E; ++a) {
         double v = 0.0;
 #pragma unroll
-        for (int b = 0; b < 8; ++b) v = b == pa ? A[a][b] : v;
-        colp[buf][ty + 16 * a] = v;
+        for (int b = 0; b < E; ++b) v = b == pa ? A[a][b] : v;
+        if (ty + 16 * a < p) cross[buf][ty + 16 * a] = v;
       }
     }
     __syncthreads();
-    const double piv = rowp[buf][p];
+    const double piv = cross[buf][p];
     if (threadIdx.x == 0 && !(piv > 0.0)) atomicExch(bad, 1);
     const double d = 1.0 / piv;
-    double rj[8], fi[8];
+    double ui[E], uj[E], fi[E], rj[E];
 #pragma unroll
-    for (int b = 0; b < 8; ++b) rj[b] = rowp[buf][tx + 16 * b];
+    for (int a = 0; a < E; ++a) {
+      ui[a] = cross[buf][ty + 16 * a];
+      fi[a] = ui[a] * d;  // column p, scaled
+    }
 #pragma unroll
-    for (int a = 0; a < 8; ++a) fi[a] = colp[buf][ty + 16 * a] * d;
+    for (int b = 0; b < E; ++b) {
+      uj[b] = cross[buf][tx + 16 * b];
+      rj[b] = tx + 16 * b < p ? -uj[b] : uj[b];  // row p
+    }
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
+    for (int a = 0; a < E; ++a)
 #pragma unroll
-      for (int b = 0; b < 8; ++b) A[a][b] = fma(-fi[a], rj[b], A[a][b]);
-    // row p, column p and the pivot itself
+      for (int b = a + 1; b < E; ++b) A[a][b] = fma(-fi[a], rj[b], A[a][b]);
+    if (ty <= tx) {
+#pragma unroll
+      for (int a = 0; a < E; ++a) A[a][a] = fma(-fi[a], rj[a], A[a][a]);
+    }
+    // row p (k > p): u d; column p (k < p): -u d; the pivot: d
     if (ty == pr) {
 #pragma unroll
-      for (int a = 0; a < 8; ++a)
+      for (int a = 0; a < E; ++a)
         if (a == pa)
 #pragma unroll
-          for (int b = 0; b < 8; ++b) A[a][b] = rj[b] * d;
+          for (int b = 0; b < E; ++b) {
+            const int j = tx + 16 * b;
+            if (j > p) A[a][b] = uj[b] * d;
+            else if (j == p) A[a][b] = d;
+          }
     }
     if (tx == pr) {
 #pragma unroll
-      for (int b = 0; b < 8; ++b)
+      for (int b = 0; b < E; ++b)
         if (b == pa)
 #pragma unroll
-          for (int a = 0; a < 8; ++a) A[a][b] = (ty + 16 * a == p) ? d : -fi[a];
+          for (int a = 0; a < E; ++a)
+            if (ty + 16 * a < p) A[a][b] = -ui[a] * d;
     }
   }
-  // symmetric by construction up to rounding: average the two triangles
-  extern __shared__ float tr[];  // 128 x 129
+  // the upper triangle is the inverse; write it and its mirror (through a
+  // shared-memory transpose, so the stores stay row-contiguous)
+  extern __shared__ float tr[];  // D x (D + 1)
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
+  for (int a = 0; a < E; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) tr[(ty + 16 * a) * 129 + tx + 16 * b] = (float)A[a][b];
+    for (int b = 0; b < E; ++b) tr[(ty + 16 * a) * (D + 1) + tx + 16 * b] = (float)A[a][b];
   __syncthreads();
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
+  for (int a = 0; a < E; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) {
+    for (int b = 0; b < E; ++b) {
       const int i = ty + 16 * a, j = tx + 16 * b;
       if (i < s && j < s) {
-        const float v = (float)(0.5 * (A[a][b] + (double)tr[j * 129 + i]));
+        const float v = i <= j ? tr[i * (D + 1) + j] : tr[j * (D + 1) + i];
         V[i * ld + j] = v;
         store_split(S, i * ld + j, lo, v);
       }
     }
 }
 
-cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st) {
-  const int smem = 128 * 129 * 4;
-  cudaError_t e = cudaFuncSetAttribute(spd_block_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+template <int D>
+static cudaError_t spd_block_launch(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st) {
+  const int smem = D * (D + 1) * 4;
+  cudaError_t e = cudaFuncSetAttribute(spd_block_inverse_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  spd_block_inverse_kernel<<<1, 256, smem, st>>>(V, S, ld, lo, s, bad);
+  spd_block_inverse_kernel<D><<<1, 256, smem, st>>>(V, S, ld, lo, s, bad);
   return cudaGetLastError();
+}
+
+cudaError_t launch_spd_block_inverse(float* V, float* S, int64_t ld, int64_t lo, int s, int* bad, cudaStream_t st) {
+  if (s <= 64) return spd_block_launch<64>(V, S, ld, lo, s, bad, st);
+  if (s <= 96) return spd_block_launch<96>(V, S, ld, lo, s, bad, st);
+  return cudaErrorInvalidValue;
 }
 
 

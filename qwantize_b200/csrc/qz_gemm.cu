@@ -1159,7 +1159,7 @@ static int tf3_gemm(const SpdWork& w, const CUtensorMap& ma, int ax, int ay, con
 
 static int spd_inverse_rec(const SpdWork& w, int64_t off, int64_t s) {
   const int64_t n = w.n;
-  if (s <= 128)
+  if (s <= 96)
     return cuda_status(launch_spd_block_inverse(w.V + off * n + off, w.S + off * n + off, n, n * n, (int)s, w.bad,
                                                 w.st), "spd block inverse");
   const int64_t s1 = (s / 32 + 1) / 2 * 32, s2 = s - s1, o2 = off + s1;
