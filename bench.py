@@ -705,7 +705,8 @@ def extras(ws, rank, device, peak_tf, args):
 def profile_call(spec):
     """Three launches of one quantization of the config-1 weight (native
     outputs), for ncu captures of a single kernel: spec "fmt,bs,method", e.g.
-    "nvfp4,16,optimal" or "int8,32,optimal"; "gram" runs three full Grams of
+    "nvfp4,16,optimal" or "int8,32,optimal" ("hoptimal": the Hessian search with
+    H blocks from 65,536 config-2 tokens); "gram" runs three full Grams of
     65,536 tokens, "gptq" one GPTQ of the config weight."""
     from qwantize_b200 import _lib
     from qwantize_b200.synthetic import make_weight_device
@@ -731,10 +732,22 @@ def profile_call(spec):
         return
     fmt, bs, meth = spec.split(",")
     fmt = {"nvfp4": 0, "mxfp4": 1, "nvint4": 3, "int8": 4}[fmt]
-    bs, meth = int(bs), {"naive": 0, "optimal": 1}[meth]
+    bs, meth = int(bs), {"naive": 0, "optimal": 1, "hoptimal": 2}[meth]
     dev = torch.device("cuda", 0)
     L = _lib.load()
     W = make_weight_device(M, K, 0, dev)
+    if meth == 2:  # Hessian search: H blocks from 65,536 config-2 tokens
+        from qwantize_b200.hessian import gram
+        from qwantize_b200.synthetic import make_activations
+        Hb = gram(make_activations(65536, K, seed=1, device=dev), "blockdiag", bs)
+        codes = torch.empty(WEIGHTS // bs, dtype=torch.uint8, device=dev)
+        packed = torch.empty(WEIGHTS, dtype=torch.uint8, device=dev)
+        sp = torch.cuda.current_stream(dev).cuda_stream
+        for _ in range(3):
+            _lib.check(L.qz_quantize(W.data_ptr(), 1, WEIGHTS // bs, bs, fmt, meth, Hb.data_ptr(), K // bs, None,
+                                     None, None, codes.data_ptr(), packed.data_ptr(), None, sp), "qz_quantize")
+        torch.cuda.synchronize(dev)
+        return
     codes = torch.empty(WEIGHTS // bs, dtype=torch.uint8, device=dev)
     packed = torch.empty(WEIGHTS, dtype=torch.uint8, device=dev)
     dq = torch.empty(WEIGHTS, dtype=torch.bfloat16, device=dev)
@@ -763,7 +776,7 @@ def main():
                     help="tokens for config 4's full 28672^2 Gram (0 skips it)")
     ap.add_argument("--profile-call", default=None,
                     help='only launch one quantization three times (ncu captures), e.g. "int8,32,optimal"; '
-                         '"gram" three full Grams of 65,536 tokens, "gptq" one GPTQ of the config weight')
+                         '"nvfp4,16,hoptimal" the Hessian search, "gram" three full Grams of 65,536 tokens, "gptq" one GPTQ of the config weight')
     args = ap.parse_args()
     if args.profile_call:
         profile_call(args.profile_call)
