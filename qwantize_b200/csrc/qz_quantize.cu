@@ -490,20 +490,28 @@ __device__ __forceinline__ float block_hess_ilp(const float (&x)[BS], const floa
   float acc8[8];
 #pragma unroll
   for (int g = 0; g < BS; g += 16) {
-    float acc[16];
+    // rows (g + 2k, g + 2k + 1) as one packed pair: fma.rn.f32x2 is two
+    // independent single-rounding FMAs, the scalar chains bit for bit
+    uint64_t acc2[8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
+    for (int k = 0; k < 8; ++k) acc2[k] = 0ull;
 #pragma unroll
     for (int b = 0; b < BS; ++b) {
       const uint32_t hrow = smem_u32(Ht + b * BS + g);
+      const uint64_t rb = pk2(r[b], r[b]);
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         const float4 h = lds_f4(hrow + 16 * q4);
-        acc[4 * q4 + 0] = __fmaf_rn(h.x, r[b], acc[4 * q4 + 0]);
-        acc[4 * q4 + 1] = __fmaf_rn(h.y, r[b], acc[4 * q4 + 1]);
-        acc[4 * q4 + 2] = __fmaf_rn(h.z, r[b], acc[4 * q4 + 2]);
-        acc[4 * q4 + 3] = __fmaf_rn(h.w, r[b], acc[4 * q4 + 3]);
+        acc2[2 * q4 + 0] = fma2(pk2(h.x, h.y), rb, acc2[2 * q4 + 0]);
+        acc2[2 * q4 + 1] = fma2(pk2(h.z, h.w), rb, acc2[2 * q4 + 1]);
       }
+    }
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float2 v = up2(acc2[k]);
+      acc[2 * k] = v.x;
+      acc[2 * k + 1] = v.y;
     }
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
@@ -1291,7 +1299,7 @@ __global__ void __launch_bounds__(kThreads, MinCtas<BS, FMT, METHOD>::v)
 // shared memory.  Each thread walks its block's candidates in ascending order
 // with the reference's fast-fail rule, which does depend on the running best.
 template <int BS, int FMT, int DT>
-__global__ void __launch_bounds__(128) hessian_kernel(QuantArgs p) {
+__global__ void __launch_bounds__(128, BS == 32 ? 3 : 1) hessian_kernel(QuantArgs p) {
   constexpr int MODE = Mode<FMT, DT>::v;
   __shared__ __align__(16) float Ht[BS * BS];
   const int64_t j = blockIdx.x;
