@@ -1355,21 +1355,29 @@ __device__ __forceinline__ float quant_unit(float v) {  // fp4_quantize(v, 1)
 
 // y = A v with A^T in shared memory (At[b*BS + a] = A[a][b]); every y[a] is a
 // sequential FMA chain over b ascending.
+// The chains of (y[2k], y[2k+1]) run as one packed fma.rn.f32x2 pair (two
+// single-rounding FMAs: the scalar chains bit for bit).
 template <int BS>
 __device__ __forceinline__ void matvec_t(const float* __restrict__ At, const float (&v)[BS], float (&y)[BS]) {
+  uint64_t y2[BS / 2];
 #pragma unroll
-  for (int k = 0; k < BS; ++k) y[k] = 0.0f;
+  for (int k = 0; k < BS / 2; ++k) y2[k] = 0ull;
 #pragma unroll
   for (int b = 0; b < BS; ++b) {
     const uint32_t row = smem_u32(At + b * BS);
+    const uint64_t vb = pk2(v[b], v[b]);
 #pragma unroll
     for (int q4 = 0; q4 < BS / 4; ++q4) {
       const float4 h = lds_f4(row + 16 * q4);
-      y[4 * q4 + 0] = __fmaf_rn(h.x, v[b], y[4 * q4 + 0]);
-      y[4 * q4 + 1] = __fmaf_rn(h.y, v[b], y[4 * q4 + 1]);
-      y[4 * q4 + 2] = __fmaf_rn(h.z, v[b], y[4 * q4 + 2]);
-      y[4 * q4 + 3] = __fmaf_rn(h.w, v[b], y[4 * q4 + 3]);
+      y2[2 * q4 + 0] = fma2(pk2(h.x, h.y), vb, y2[2 * q4 + 0]);
+      y2[2 * q4 + 1] = fma2(pk2(h.z, h.w), vb, y2[2 * q4 + 1]);
     }
+  }
+#pragma unroll
+  for (int k = 0; k < BS / 2; ++k) {
+    const float2 t = up2(y2[k]);
+    y[2 * k] = t.x;
+    y[2 * k + 1] = t.y;
   }
 }
 
