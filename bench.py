@@ -653,13 +653,17 @@ def extras(ws, rank, device, peak_tf, args):
     q.nvfp4_optimal(Wc, return_dequant=True)
     torch.cuda.synchronize()
     reps = 5
+    kept = []  # a caller quantizing a model keeps every result
     t_d = time.perf_counter()
     for _ in range(reps):
-        s_, q_, d_ = q.nvfp4_optimal(Wc, return_dequant=True)
+        kept.append(q.nvfp4_optimal(Wc, return_dequant=True))
     torch.cuda.synchronize()
     ms_d = (time.perf_counter() - t_d) * 1e3 / reps
+    s_, q_, d_ = kept[-1]
+    del kept
     out["dropin_fp32_e2e"] = {
-        "call": "nvfp4_optimal(W_cpu, return_dequant=True), bs16, 2560x9728 bf16 pageable host weight",
+        "call": "nvfp4_optimal(W_cpu, return_dequant=True), bs16, 2560x9728 bf16 pageable host weight, "
+                "results kept (pageable CPU tensors)",
         "ms": ms_d, "gweights_per_s": n_w / (ms_d / 1e3) / 1e9,
         "h2d_bytes": n_w * 2, "d2h_bytes": n_w * 8 + n_w // 16 * 4, "timing": "host wall clock, synchronized"}
     del W_cpu, Wc, s_, q_, d_, W, Wb, Hb

@@ -11,6 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib as L
+from . import _staging
 
 
 def cuda_device(t: torch.Tensor) -> torch.device:
@@ -30,7 +31,7 @@ def _blocks(W: torch.Tensor, dim: int, valid=(16, 32)):
     batch_shape = x.shape[:-1]
     if x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
         x = x.float()  # W.float() in the reference: float64 etc. round once to fp32
-    x = x.to(dev, non_blocking=True).reshape(-1, block_size)
+    x = (_staging.to_device(x, dev) if x.device.type == "cpu" else x.to(dev)).reshape(-1, block_size)
     if not x.is_contiguous():
         x = x.contiguous()
     if x.data_ptr() % 16:  # a view at an odd offset: the kernels load 16-byte vectors
@@ -62,18 +63,11 @@ def quantize_fp32(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(16,
 
 def to_host_like(res, want, dev):
     """Return device results on `want`: unchanged on the GPU; for a CPU caller
-    the copies go to page-locked host tensors (PyTorch's cached pinned
-    allocator, so repeated calls reuse them) at full PCIe speed, all issued
-    before one synchronisation of the stream."""
+    ordinary CPU tensors, copied through the library's page-locked staging
+    buffers (qwantize_b200._staging) in order after the call's kernels."""
     if want.type != "cpu":
         return tuple(t.to(want) for t in res)
-    out = []
-    for t in res:
-        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-        h.copy_(t, non_blocking=True)
-        out.append(h)
-    torch.cuda.current_stream(dev).synchronize()
-    return tuple(out)
+    return _staging.to_host(res, dev)
 
 
 def quantize_native(W, dim, return_dequant, fmt, method, H_blocks=None, valid=(16, 32)):
@@ -155,22 +149,6 @@ def admm_fp32(W, dim, return_dequant, H, Hn, Minv, n_outer=3, n_inner=10, rho=1.
     if return_dequant:
         res = res + (dq.reshape(*batch_shape, bs).movedim(-1, dim),)
     return to_host_like(res, W.device, dev)
-
-
-def to_host_like(res, want, dev):
-    """Return device results on `want`: unchanged on the GPU; for a CPU caller
-    the copies go to page-locked host tensors (PyTorch's cached pinned
-    allocator, so repeated calls reuse them) at full PCIe speed, all issued
-    before one synchronisation of the stream."""
-    if want.type != "cpu":
-        return tuple(t.to(want) for t in res)
-    out = []
-    for t in res:
-        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-        h.copy_(t, non_blocking=True)
-        out.append(h)
-    torch.cuda.current_stream(dev).synchronize()
-    return tuple(out)
 
 
 def quantize_many(weights, fmt, method, block_size=16, packed=True, return_dequant=False, outputs=None):
