@@ -178,7 +178,8 @@ def quantize_many(weights, fmt, method, block_size=16, packed=True, return_dequa
     for i, W in enumerate(weights):
         assert W.dtype == dt, "all weights of a grouped call share one dtype"
         assert W.shape[-1] % block_size == 0, f"last dimension {W.shape[-1]} is not a multiple of {block_size}"
-        x = W.to(dev, non_blocking=True).contiguous().reshape(-1, block_size)
+        x = (_staging.to_device(W, dev) if W.device.type == "cpu" else W.to(dev).contiguous()).reshape(
+            -1, block_size)
         if x.data_ptr() % 16:
             x = x.clone()
         N = x.shape[0]
@@ -207,6 +208,8 @@ def quantize_many(weights, fmt, method, block_size=16, packed=True, return_dequa
         results.append(out)
     L.check(L.load().qz_quantize_grouped(items, len(weights), L.dtype_code(x.dtype), block_size, fmt, method,
                                          L.stream_ptr(dev)), "qz_quantize_grouped")
-    if weights[0].device != dev:
+    if weights[0].device.type == "cpu":
+        results = [_staging.to_host(r, dev) for r in results]
+    elif weights[0].device != dev:
         results = [tuple(t.to(weights[0].device) for t in r) for r in results]
     return results

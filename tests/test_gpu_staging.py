@@ -49,3 +49,19 @@ def test_dropin_cpu_input_matches_device_input(dim):
     for c, g in zip(cpu, gpu):
         assert torch.equal(c, g.cpu())
     assert torch.equal(again[0], q.mxfp4_naive(W.to(DEV), dim=dim)[0].cpu())
+
+
+def test_quantize_many_cpu_inputs():
+    """The grouped call on CPU weights returns CPU results equal to the same
+    call on device weights."""
+    from qwantize_b200.core import quantize_many
+    from qwantize_b200 import _lib
+    from qwantize_b200.synthetic import make_weight
+    ws = [make_weight(m, 512, 10 + m) for m in (1, 37, 256)]
+    for packed in (True, False):
+        cpu = quantize_many(ws, _lib.FMT_NVFP4, _lib.METHOD_SSE, 16, packed=packed, return_dequant=True)
+        gpu = quantize_many([w.to(DEV) for w in ws], _lib.FMT_NVFP4, _lib.METHOD_SSE, 16, packed=packed,
+                            return_dequant=True)
+        for rc, rg in zip(cpu, gpu):
+            for c, g in zip(rc, rg):
+                assert c.device.type == "cpu" and torch.equal(c, g.cpu())
