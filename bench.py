@@ -603,8 +603,17 @@ def extras(ws, rank, device, peak_tf, args):
     ms_full = _max_over_ranks(_ev_time(lambda: gram(X, "full", out=H), stream, 3), ws, device)
     ar_ms = None
     if ws > 1:
+        # the reduction of distributed.gram_sharded: the upper 256 x 256 tiles
+        # (about half of H) all-reduced, then expanded to the symmetric H
+        from qwantize_b200.hessian import unpack_upper_tiles
+        P = gram(X, "upper_tiles")
+
+        def reduce_full():
+            torch.distributed.all_reduce(P)
+            unpack_upper_tiles(P, Kx, out=H)
         _barrier(ws)
-        ar_ms = _max_over_ranks(_ev_time(lambda: torch.distributed.all_reduce(H), stream, 3), ws, device)
+        ar_ms = _max_over_ranks(_ev_time(reduce_full, stream, 3), ws, device)
+        del P
     flop = T * Kx * (Kx + 1)
     out["config2_gram"] = {
         "tokens": T, "K": Kx, "ms_full": ms_full, "tflops_full_whole_job": flop / ms_full / 1e9,
@@ -614,6 +623,7 @@ def extras(ws, rank, device, peak_tf, args):
         "frac_of_measured_bf16_peak_burst": flop / ms_full / 1e9 / ws / peak_tf[0],
         "ms_blockdiag": ms_diag, "blockdiag_GBps": 2 * (t1 - t0) * Kx / ms_diag / 1e6,
         "allreduce_full_H_ms": ar_ms, "allreduce_blockdiag_H_ms": ar_bd,
+        "full_H_reduction": "upper 256x256 tiles all-reduced (about half of H), then expanded",
         "sharding": f"tokens over {ws} rank(s), whole 65536-token chunks"}
     _, _, dq = q.nvfp4_optimal(Wb, return_dequant=True)
     dqb = dq.reshape(2560, Kx).to(torch.bfloat16)
@@ -681,8 +691,15 @@ def extras(ws, rank, device, peak_tf, args):
         ms_g4 = _max_over_ranks(_ev_time(lambda: gram(X4, "full", out=H4), stream, 2), ws, device)
         ar4 = None
         if ws > 1:
+            from qwantize_b200.hessian import unpack_upper_tiles
+            P4 = gram(X4, "upper_tiles")
+
+            def reduce_full4():
+                torch.distributed.all_reduce(P4)
+                unpack_upper_tiles(P4, K4, out=H4)
             _barrier(ws)
-            ar4 = _max_over_ranks(_ev_time(lambda: torch.distributed.all_reduce(H4), stream), ws, device)
+            ar4 = _max_over_ranks(_ev_time(reduce_full4, stream), ws, device)
+            del P4
         del X4
         torch.cuda.empty_cache()
         W4 = make_weight_device(M4, K4, 7, device).reshape(M4, K4 // 16, 16)
@@ -698,7 +715,9 @@ def extras(ws, rank, device, peak_tf, args):
         out["config4_hopt_down_proj"] = {
             "tokens": T4, "K": K4, "M": M4, "ms_full_gram": ms_g4, "tflops_full_per_gpu": f4 / ms_g4 / 1e9 / ws,
             "frac_of_measured_bf16_peak_sustained": f4 / ms_g4 / 1e9 / ws / peak_tf[1],
-            "allreduce_full_H_ms": ar4, "H_bytes": K4 * K4 * 4, "nvfp4_search_ms": ms_s4,
+            "allreduce_full_H_ms": ar4, "H_bytes": K4 * K4 * 4,
+            "allreduced_bytes": ((K4 + 255) // 256) * ((K4 + 255) // 256 + 1) // 2 * 65536 * 4,
+            "nvfp4_search_ms": ms_s4,
             "total_ms": tot, "gweights_per_s": M4 * K4 / (tot / 1e3) / 1e9,
             "sharding": f"tokens over {ws} rank(s) for H, rows for the search"}
         del H4, Hb4, W4

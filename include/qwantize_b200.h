@@ -66,6 +66,7 @@ extern "C" {
 /* Gram modes */
 #define QZ_GRAM_FULL 0      /* H = X^T X, (K, K) fp32, symmetric */
 #define QZ_GRAM_BLOCKDIAG 1 /* H_j = X_j^T X_j, (K/bs, bs, bs) fp32 */
+#define QZ_GRAM_FULL_UPPER_TILES 2 /* the 256 x 256 tiles of X^T X on and above the diagonal, packed */
 
 /*
  * qz_quantize -- per-block scale selection + E2M1 quantization in one pass.
@@ -185,9 +186,22 @@ QZ_API int qz_fp4_unpack(const uint8_t* packed, int64_t n_bytes, int8_t* out, vo
  * (also nvfp4/kernels.py:386-397, mxfp4/reference.py:271-284).
  * QZ_GRAM_FULL writes the symmetric (K, K) matrix; QZ_GRAM_BLOCKDIAG writes
  * (K/bs, bs, bs).  accumulate != 0 adds into H instead of overwriting it.
+ * QZ_GRAM_FULL_UPPER_TILES writes only the t(t+1)/2 tiles of 256 x 256 on and
+ * above the diagonal (t = ceil(K / 256)) into H, t(t+1)/2 * 65536 floats:
+ * tile (mi, nj >= mi) at index mi*t - mi*(mi-1)/2 + (nj - mi), each tile
+ * column-major (element (r, c) at c*256 + r), entries beyond K zero.  It is
+ * about half of the full matrix, so a token-sharded Gram all-reduces it and
+ * expands it with qz_gram_unpack (same sums, bit for bit, as QZ_GRAM_FULL).
  */
 QZ_API int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int block_size, int accumulate,
             float* H, void* stream);
+
+/*
+ * qz_gram_unpack -- the symmetric (K, K) H from the packed upper tiles of
+ * qz_gram (QZ_GRAM_FULL_UPPER_TILES).  Added beside the reference's Hessian
+ * build (nvfp4/reference.py:304-317) for the token-sharded all-reduce.
+ */
+QZ_API int qz_gram_unpack(const float* packed, int64_t K, float* H, void* stream);
 
 /*
  * qz_gram_full_noalloc -- the full Gram H = X^T X of qz_gram (QZ_GRAM_FULL),

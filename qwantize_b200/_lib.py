@@ -19,7 +19,7 @@ DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FMT_NVFP4, FMT_MXFP4 = 0, 1
 FMT_NVINT4, FMT_INT8 = 3, 4  # symmetric integer grids (nvint4/, int8/ of the reference)
 METHOD_NAIVE, METHOD_SSE, METHOD_HESSIAN, METHOD_NAIVE_ARGMIN, METHOD_TWO_ARGMIN = 0, 1, 2, 3, 4
-GRAM_FULL, GRAM_BLOCKDIAG = 0, 1
+GRAM_FULL, GRAM_BLOCKDIAG, GRAM_FULL_UPPER_TILES = 0, 1, 2
 
 # every symbol include/qwantize_b200.h declares
 EXPORTS = [
@@ -27,6 +27,7 @@ EXPORTS = [
     "qz_weight_error_sums", "qz_output_error_sums", "qz_scale_table", "qz_last_error",
     "qz_version", "qz_device_ok", "qz_poll_device_error", "qz_gram_full_noalloc", "qz_admm",
     "qz_quantize_table", "qz_selftest_wait", "qz_quantize_grouped", "qz_gptq", "qz_spd_inverse",
+    "qz_gram_unpack",
 ]
 
 
@@ -68,6 +69,7 @@ def load():
     L.qz_selftest_wait.argtypes = [ctypes.c_uint64, vp]
     L.qz_quantize_grouped.argtypes = [vp, i32, i32, i32, i32, i32, vp]
     L.qz_spd_inverse.argtypes = [vp, i64, vp, vp, vp]
+    L.qz_gram_unpack.argtypes = [vp, i64, vp, vp]
     L.qz_gptq.argtypes = [vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp]
     L.qz_last_error.restype = ctypes.c_char_p
     for name in EXPORTS:

@@ -100,6 +100,7 @@ struct GemmParams {
   // segments (last_seg, last_seg + 1, ...) of their tile
   int64_t tail_start, tail_tiles, tail_tile0, tail_r0, tail_piece_rows, last_seg;
   float* H;
+  float* packed;        // kGramFull: when set, the upper 256 x 256 tiles instead of H (column-major tiles)
   float* partials;      // kGramDiag: splits-1 partial (K/bs, bs, bs) buffers
   double* sums;
   uint32_t lbo, sbo;    // MN-major descriptor offsets (bytes)
@@ -661,8 +662,23 @@ __global__ void __launch_bounds__(Geo<MODE>::kThreads, 1)
         const bool add = u.seg > 0 || p.accumulate;
         const int64_t i = mi * G::BM + half * 128 + row;
         const int64_t j0 = nj * BN;
+        // packed upper tiles: tile (mi, nj) at its upper-triangle index, element
+        // (r, c) at c * 256 + r, so the lanes (consecutive rows) store together
+        float* tile = p.packed ? p.packed + (mi * p.tiles_n - mi * (mi - 1) / 2 + (nj - mi)) * 65536 +
+                                     half * 128 + row
+                               : nullptr;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = 0; tile && c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            float* d = tile + (int64_t)(c + q) * 256;
+            *d = add ? v[q] + *d : v[q];
+          }
+        }
+#pragma unroll 1
+        for (int c = 0; !tile && c < BN; c += 16) {
           float v[16];
           tmem_ld16(taddr + c, v);
           if (i >= p.K) continue;
@@ -872,6 +888,31 @@ static int64_t full_gram_tiles(int64_t K) {
 // into H in order (further segments of that tile), so the result stays
 // deterministic; the order costs m epilogues in a row, so m balances the
 // piece length against m epilogues (about kGramEpilogueRows rows each).
+// H (K x K) from the packed upper tiles: one 32 x 32 block of H per CTA, read
+// as the block U(min, max) of the upper triangle (coalesced along the packed
+// tiles' columns) and written row-major, transposed below the diagonal.
+__global__ void __launch_bounds__(256) gram_unpack_kernel(const float* __restrict__ P, int64_t K, int64_t t,
+                                                          float* __restrict__ H) {
+  __shared__ float sb[32][33];
+  const int64_t bi = blockIdx.y, bj = blockIdx.x;
+  const int64_t ur = bi < bj ? bi : bj, uc = bi < bj ? bj : bi;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int cc = ty; cc < 32; cc += 8) {
+    const int64_t a = ur * 32 + tx, b = uc * 32 + cc;
+    float v = 0.0f;
+    if (a < K && b < K) {
+      const int64_t mi = a >> 8, nj = b >> 8;
+      v = P[(mi * t - mi * (mi - 1) / 2 + (nj - mi)) * 65536 + (b & 255) * 256 + (a & 255)];
+    }
+    sb[tx][cc] = v;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t i = bi * 32 + r, j = bj * 32 + tx;
+    if (i < K && j < K) H[i * K + j] = i <= j ? sb[r][tx] : sb[tx][r];
+  }
+}
+
 static void full_gram_params(GemmParams& p, int64_t T, int64_t K, int sms) {
   p.tiles_m = p.tiles_n = (K + 255) / 256;
   const int64_t n = full_gram_tiles(K);
@@ -906,7 +947,8 @@ using namespace qz;
 
 extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int block_size, int accumulate,
                        float* H, void* stream) {
-  if (mode != QZ_GRAM_FULL && mode != QZ_GRAM_BLOCKDIAG) return fail(QZ_ERR_INVALID, "unknown gram mode %d", mode);
+  if (mode != QZ_GRAM_FULL && mode != QZ_GRAM_BLOCKDIAG && mode != QZ_GRAM_FULL_UPPER_TILES)
+    return fail(QZ_ERR_INVALID, "unknown gram mode %d", mode);
   if (T < 0 || K <= 0) return fail(QZ_ERR_INVALID, "need T >= 0 and K > 0");
   if (K % 8 != 0) return fail(QZ_ERR_INVALID, "K must be a multiple of 8 (16-byte rows for TMA)");
   if (mode == QZ_GRAM_BLOCKDIAG &&
@@ -915,7 +957,8 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   if (K > 2147483647LL || T > 2147483647LL) return fail(QZ_ERR_INVALID, "T and K must fit in int32");
   if (!H) return fail(QZ_ERR_INVALID, "H is NULL");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t n_out = mode == QZ_GRAM_FULL ? K * K : K * block_size;
+  const int64_t n_out = mode == QZ_GRAM_FULL ? K * K
+                        : mode == QZ_GRAM_FULL_UPPER_TILES ? full_gram_tiles(K) * 65536 : K * block_size;
   if (T == 0) {
     if (accumulate) return QZ_OK;
     return cuda_status(cudaMemsetAsync(H, 0, (size_t)n_out * 4, st), "cudaMemsetAsync");
@@ -930,7 +973,8 @@ extern "C" int qz_gram(const uint16_t* X, int64_t T, int64_t K, int mode, int bl
   int sms = 0;
   int s = current_sms(&sms);
   if (s != QZ_OK) return s;
-  if (mode == QZ_GRAM_FULL) {
+  if (mode == QZ_GRAM_FULL || mode == QZ_GRAM_FULL_UPPER_TILES) {
+    if (mode == QZ_GRAM_FULL_UPPER_TILES) p.packed = H;
     // One persistent launch over (segment, tile) units, segment-major: all CTAs
     // sweep the same token rows at about the same time, so the column panels
     // they share stay in L2.  A tile's segments are added in segment order
@@ -1018,6 +1062,14 @@ extern "C" int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, con
   p.tiles_n = (M + 127) / 128;
   p.n_tiles = p.tiles_m * p.tiles_n;
   return launch_gemm<kMetrics>(mx, mw, mq, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qz_gram_unpack(const float* packed, int64_t K, float* H, void* stream) {
+  if (K <= 0 || (K + 31) / 32 > 65535) return fail(QZ_ERR_INVALID, "need 0 < K <= 2097120, got %lld", (long long)K);
+  if (!packed || !H) return fail(QZ_ERR_INVALID, "NULL pointer");
+  const unsigned nb = (unsigned)((K + 31) / 32);
+  gram_unpack_kernel<<<dim3(nb, nb), 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, K, (K + 255) / 256, H);
+  return cuda_status(cudaGetLastError(), "gram unpack launch");
 }
 
 extern "C" int qz_gram_full_noalloc(const uint16_t* X, int64_t T, int64_t K, int accumulate, float* H,

@@ -98,14 +98,22 @@ def quantize_sharded(fn: Callable, W: torch.Tensor, dim: int = -1, return_dequan
 
 
 def gram_sharded(X_local: torch.Tensor, mode: str = "full", block_size: int = 16, group=None,
-                 gram_fn: Optional[Callable] = None) -> torch.Tensor:
+                 gram_fn: Optional[Callable] = None, unpack_fn: Optional[Callable] = None) -> torch.Tensor:
     """H = X^T X over the tokens of all ranks: the local Gram of this rank's
     rows, then one all-reduce (sum, fp32).  mode "full" -> (K, K),
-    "blockdiag" -> (K/bs, bs, bs)."""
+    "blockdiag" -> (K/bs, bs, bs).  For "full" over several ranks the ranks
+    reduce only the 256 x 256 tiles on and above the diagonal (gram mode
+    "upper_tiles", about half of H's bytes over NVLink) and expand the sum
+    with unpack_fn(packed, K); the sums are the same, bit for bit."""
     if gram_fn is None:
-        from .hessian import gram as gram_fn
-    H = gram_fn(X_local, mode, block_size)
+        from .hessian import gram as gram_fn, unpack_upper_tiles
+        unpack_fn = unpack_fn or unpack_upper_tiles
     _, world = _group_info(group)
+    if mode == "full" and world > 1 and unpack_fn is not None:
+        P = gram_fn(X_local, "upper_tiles", block_size)
+        dist.all_reduce(P, op=dist.ReduceOp.SUM, group=group)
+        return unpack_fn(P, X_local.shape[1])
+    H = gram_fn(X_local, mode, block_size)
     if world > 1:
         dist.all_reduce(H, op=dist.ReduceOp.SUM, group=group)
     return H

@@ -13,12 +13,14 @@ from .core import cuda_device
 def gram(X: torch.Tensor, mode: str = "full", block_size: int = 16, out: torch.Tensor = None,
          accumulate: bool = False) -> torch.Tensor:
     """H = X^T X in fp32 for bf16 X (T, K).  mode "full" -> (K, K);
-    "blockdiag" -> (K/bs, bs, bs)."""
+    "blockdiag" -> (K/bs, bs, bs); "upper_tiles" -> the 256 x 256 tiles on and
+    above the diagonal, packed (t(t+1)/2, 256, 256), t = ceil(K / 256), each
+    tile column-major (expand with unpack_upper_tiles)."""
     assert X.ndim == 2
     dev = cuda_device(X)
     Xd = X.to(dev, torch.bfloat16).contiguous()
     T, K = Xd.shape
-    m = L.GRAM_FULL if mode == "full" else L.GRAM_BLOCKDIAG
+    m = {"full": L.GRAM_FULL, "blockdiag": L.GRAM_BLOCKDIAG, "upper_tiles": L.GRAM_FULL_UPPER_TILES}[mode]
     if m == L.GRAM_BLOCKDIAG and block_size > 128:
         # blocks wider than one 128-column diagonal tile: the full Gram of each
         # contiguous column slice
@@ -35,6 +37,9 @@ def gram(X: torch.Tensor, mode: str = "full", block_size: int = 16, out: torch.T
     if m == L.GRAM_BLOCKDIAG:
         assert K % block_size == 0
         shape = (K // block_size, block_size, block_size)
+    elif m == L.GRAM_FULL_UPPER_TILES:
+        t = (K + 255) // 256
+        shape = (t * (t + 1) // 2, 256, 256)
     else:
         shape = (K, K)
     if out is None:
@@ -43,6 +48,18 @@ def gram(X: torch.Tensor, mode: str = "full", block_size: int = 16, out: torch.T
     assert tuple(out.shape) == shape and out.dtype == torch.float32 and out.is_contiguous()
     L.check(L.load().qz_gram(L.ptr(Xd), T, K, m, block_size, int(accumulate), L.ptr(out),
                              L.stream_ptr(dev)), "qz_gram")
+    return out
+
+
+def unpack_upper_tiles(packed: torch.Tensor, K: int, out: torch.Tensor = None) -> torch.Tensor:
+    """The symmetric (K, K) H from gram(X, "upper_tiles") (qz_gram_unpack)."""
+    dev = cuda_device(packed)
+    t = (K + 255) // 256
+    assert tuple(packed.shape) == (t * (t + 1) // 2, 256, 256) and packed.is_contiguous()
+    if out is None:
+        out = torch.empty((K, K), dtype=torch.float32, device=dev)
+    assert tuple(out.shape) == (K, K) and out.dtype == torch.float32 and out.is_contiguous()
+    L.check(L.load().qz_gram_unpack(L.ptr(packed), K, L.ptr(out), L.stream_ptr(dev)), "qz_gram_unpack")
     return out
 
 

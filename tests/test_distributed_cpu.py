@@ -66,6 +66,33 @@ def _oracle_gram(X, mode, bs):
     return torch.from_numpy(H).double()  # double so sums of shards are exact enough
 
 
+def _pack_upper(H):
+    """The layout of qz_gram's QZ_GRAM_FULL_UPPER_TILES: tiles (mi, nj >= mi)
+    of 256 x 256 in upper-triangle order, each column-major, zero beyond K."""
+    K = H.shape[0]
+    t = (K + 255) // 256
+    Hp = torch.zeros(t * 256, t * 256, dtype=H.dtype)
+    Hp[:K, :K] = H
+    tiles = [Hp[mi * 256:(mi + 1) * 256, nj * 256:(nj + 1) * 256].t() for mi in range(t) for nj in range(mi, t)]
+    return torch.stack(tiles).contiguous()
+
+
+def _unpack_upper(P, K):
+    t = (K + 255) // 256
+    Hp = torch.zeros(t * 256, t * 256, dtype=P.dtype)
+    k = 0
+    for mi in range(t):
+        for nj in range(mi, t):
+            Hp[mi * 256:(mi + 1) * 256, nj * 256:(nj + 1) * 256] = P[k].t()
+            k += 1
+    U = torch.triu(Hp[:K, :K])
+    return U + torch.triu(U, 1).t()
+
+
+def _oracle_gram_tiles(X, mode, bs):
+    return _pack_upper(_oracle_gram(X, "full", bs)) if mode == "upper_tiles" else _oracle_gram(X, mode, bs)
+
+
 def _worker(rank, world, port, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
@@ -85,6 +112,13 @@ def _worker(rank, world, port, out_dir):
     # per-shard partial Grams are rounded to fp32 once each: tolerance relative
     # to the largest entry
     res["gram"] = bool(((H - Href).abs() <= 1e-6 * Href.abs().max()).all())
+    # the packed upper tiles are all-reduced and expanded (K = 520: three tile
+    # rows, ragged last tiles)
+    X2 = make_activations(200, 520, seed=10, chunk_tokens=64)
+    u0, u1 = token_chunks(200, world, rank, chunk=64)
+    H2 = gram_sharded(X2[u0:u1], "full", gram_fn=_oracle_gram_tiles, unpack_fn=_unpack_upper)
+    H2ref = _oracle_gram(X2, "full", 16)
+    res["gram_tiles"] = bool(((H2 - H2ref).abs() <= 1e-6 * H2ref.abs().max()).all()) and torch.equal(H2, H2.t())
     Hb = gram_sharded(X[t0:t1], "blockdiag", 16, gram_fn=_oracle_gram)
     Hbr = _oracle_gram(X, "blockdiag", 16)
     res["gram_bd"] = bool(((Hb - Hbr).abs() <= 1e-6 * Hbr.abs().max()).all())

@@ -167,3 +167,28 @@ def test_admm_kernel_vs_oracle_and_reference(oracle, bs):
     same = (s2.cpu().numpy().reshape(-1) == g[f"admm_X_{bs}_scales"].reshape(-1)).mean()
     assert same >= 0.99, same
     assert torch.equal(dq2.cpu(), q2.cpu() * s2.cpu().unsqueeze(-1))
+
+
+@pytest.mark.parametrize("T,K", [(3000, 1000), (300000, 520), (5000, 9728), (64, 256)])
+def test_gram_upper_tiles_unpack_equals_full(T, K):
+    """QZ_GRAM_FULL_UPPER_TILES + qz_gram_unpack gives QZ_GRAM_FULL's H bit for
+    bit (ragged K, several 262,144-token segments, accumulate); the packed
+    tiles follow the documented layout (upper-triangle order, column-major)."""
+    from qwantize_b200.hessian import gram, unpack_upper_tiles
+    g = torch.Generator().manual_seed(T + K)
+    X = (torch.randn(T, K, generator=g) * torch.exp(torch.randn(K, generator=g))).to(torch.bfloat16).to(DEV)
+    H = gram(X, "full")
+    P = gram(X, "upper_tiles")
+    assert torch.equal(unpack_upper_tiles(P, K), H)
+    t = (K + 255) // 256
+    Hp = torch.zeros(t * 256, t * 256, device=DEV)
+    Hp[:K, :K] = H
+    k = 0
+    for mi in range(t):
+        for nj in range(mi, t):
+            assert torch.equal(P[k], Hp[mi * 256:(mi + 1) * 256, nj * 256:(nj + 1) * 256].t())
+            k += 1
+    # accumulate: a second Gram added into both forms
+    gram(X, "full", out=H, accumulate=True)
+    gram(X, "upper_tiles", out=P, accumulate=True)
+    assert torch.equal(unpack_upper_tiles(P, K), H)
