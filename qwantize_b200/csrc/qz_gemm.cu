@@ -888,27 +888,29 @@ static int64_t full_gram_tiles(int64_t K) {
 // into H in order (further segments of that tile), so the result stays
 // deterministic; the order costs m epilogues in a row, so m balances the
 // piece length against m epilogues (about kGramEpilogueRows rows each).
-// H (K x K) from the packed upper tiles: one 32 x 32 block of H per CTA, read
-// as the block U(min, max) of the upper triangle (coalesced along the packed
-// tiles' columns) and written row-major, transposed below the diagonal.
+// H (K x K) from the packed upper tiles: one 64 x 64 block of H per CTA, read
+// as the block U(min, max) of the upper triangle, which lies in one packed
+// tile (coalesced along the tile's columns), and written row-major,
+// transposed below the diagonal through shared memory.
 __global__ void __launch_bounds__(256) gram_unpack_kernel(const float* __restrict__ P, int64_t K, int64_t t,
                                                           float* __restrict__ H) {
-  __shared__ float sb[32][33];
+  __shared__ float sb[64][65];
   const int64_t bi = blockIdx.y, bj = blockIdx.x;
   const int64_t ur = bi < bj ? bi : bj, uc = bi < bj ? bj : bi;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int cc = ty; cc < 32; cc += 8) {
-    const int64_t a = ur * 32 + tx, b = uc * 32 + cc;
-    float v = 0.0f;
-    if (a < K && b < K) {
-      const int64_t mi = a >> 8, nj = b >> 8;
-      v = P[(mi * t - mi * (mi - 1) / 2 + (nj - mi)) * 65536 + (b & 255) * 256 + (a & 255)];
-    }
-    sb[tx][cc] = v;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  const int64_t mi = ur >> 2, nj = uc >> 2;  // four 64-blocks per 256-tile
+  const float* tile = P + (mi * t - mi * (mi - 1) / 2 + (nj - mi)) * 65536 + (ur & 3) * 64 + tx;
+  const int64_t a = ur * 64 + tx;
+#pragma unroll 4
+  for (int cc = ty; cc < 64; cc += 4) {
+    const int64_t b = uc * 64 + cc;
+    sb[tx][cc] = (a < K && b < K) ? tile[((uc & 3) * 64 + cc) * 256] : 0.0f;
   }
   __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
-    const int64_t i = bi * 32 + r, j = bj * 32 + tx;
+  const int64_t j = bj * 64 + tx;
+#pragma unroll 4
+  for (int r = ty; r < 64; r += 4) {
+    const int64_t i = bi * 64 + r;
     if (i < K && j < K) H[i * K + j] = i <= j ? sb[r][tx] : sb[tx][r];
   }
 }
@@ -1065,9 +1067,9 @@ extern "C" int qz_output_error_sums(const uint16_t* X, int64_t T, int64_t K, con
 }
 
 extern "C" int qz_gram_unpack(const float* packed, int64_t K, float* H, void* stream) {
-  if (K <= 0 || (K + 31) / 32 > 65535) return fail(QZ_ERR_INVALID, "need 0 < K <= 2097120, got %lld", (long long)K);
+  if (K <= 0 || (K + 63) / 64 > 65535) return fail(QZ_ERR_INVALID, "need 0 < K <= 4194240, got %lld", (long long)K);
   if (!packed || !H) return fail(QZ_ERR_INVALID, "NULL pointer");
-  const unsigned nb = (unsigned)((K + 31) / 32);
+  const unsigned nb = (unsigned)((K + 63) / 64);
   gram_unpack_kernel<<<dim3(nb, nb), 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, K, (K + 255) / 256, H);
   return cuda_status(cudaGetLastError(), "gram unpack launch");
 }
