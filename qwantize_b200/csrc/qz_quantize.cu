@@ -335,6 +335,50 @@ __device__ __forceinline__ float int8_sse(const float (&a)[BS], float s, float r
   return sum8<BS>(d2);
 }
 
+// The same SSE for the candidate-parallel search, where the block's |x| row
+// also sits in shared memory (row).  The loop is branch-free: it rounds
+// y = a * RN(1/s) and only records the largest |y - round(y)|; a lane whose
+// block has an element within 2^-14 of a half integer (rare) recomputes the
+// whole block from the row with IEEE quotients, out of line.  Short straight
+// code matters here: with a branch and a call site per element the kernel
+// stalled on instruction fetch.
+template <int BS>
+__device__ __noinline__ float int8_sse_exact(const float* row, float s) {
+  float acc[8];
+#pragma unroll 1
+  for (int i = 0; i < BS; i += 8) {  // torch's CPU row-sum order (sum8)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float a = row[i + k];
+      float q = __fadd_rn(__fadd_rn(__fdiv_rn(a, s), 12582912.0f), -12582912.0f);
+      q = q > 127.0f ? 127.0f : q;
+      const float d = __fsub_rn(a, __fmul_rn(q, s));
+      const float d2 = __fmul_rn(d, d);
+      acc[k] = i == 0 ? d2 : __fadd_rn(acc[k], d2);
+    }
+  }
+  float r = acc[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) r = __fadd_rn(r, acc[k]);
+  return r;
+}
+template <int BS>
+__device__ __forceinline__ float int8_sse_row(const float (&a)[BS], float s, float rc, const float* row) {
+  float d2[BS];
+  float far = 0.0f;  // largest |y - round(y)|; NaN (s = 0) is ignored, as the quotient path agrees there
+#pragma unroll
+  for (int i = 0; i < BS; ++i) {
+    const float y = __fmul_rn(a[i], rc);
+    float q = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
+    far = fmaxf(far, fabsf(__fsub_rn(y, q)));
+    q = q > 127.0f ? 127.0f : q;
+    const float d = __fsub_rn(a[i], __fmul_rn(q, s));
+    d2[i] = __fmul_rn(d, d);
+  }
+  const float E = sum8<BS>(d2);
+  return far >= 0.5f - 0x1p-14f ? int8_sse_exact<BS>(row, s) : E;
+}
+
 // Candidate SSE: the hardware path for 16-bit inputs, IEEE division for fp32.
 template <int BS, int MODE, int DT, int FMT>
 __device__ __forceinline__ float cand_sse(const float (&a)[BS], const CandTable& t, int code) {
@@ -1210,8 +1254,12 @@ __device__ __forceinline__ void quantize_cta(const Src& src, const float* table,
       // reference's E0 and bounds NaN: no candidate is ever in range.
       int lo = 1, hi = 0;
       float E0 = 0.0f;
+      float4* row = reinterpret_cast<float4*>(rows + lane * BS);
+#pragma unroll
+      for (int v = 0; v < BS / 4; ++v) row[v] = make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
       if (valid && !s_nan) {
-        E0 = base_sse<BS, MODE, DT, FMT>(a, s);
+        if constexpr (FMT == kInt8) E0 = int8_sse_row<BS>(a, s, __frcp_rn(s), rows + lane * BS);
+        else E0 = base_sse<BS, MODE, DT, FMT>(a, s);
         search_range<BS, FMT>(x, a, __uint_as_float(amax_bits), E0, lo, hi);
       }
       // Work items of CPI consecutive candidates of one block: the lookup, the
@@ -1228,9 +1276,6 @@ __device__ __forceinline__ void quantize_cta(const Src& src, const float* table,
       const int n = hi >= lo ? hi - lo + 1 : 0;
       const int n_items = (n + CPI - 1) / CPI;
 
-      float4* row = reinterpret_cast<float4*>(rows + lane * BS);
-#pragma unroll
-      for (int v = 0; v < BS / 4; ++v) row[v] = make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
       int sc = n_items;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -1257,13 +1302,24 @@ __device__ __forceinline__ void quantize_cta(const Src& src, const float* table,
           ar[4 * v] = t.x; ar[4 * v + 1] = t.y; ar[4 * v + 2] = t.z; ar[4 * v + 3] = t.w;
         }
         unsigned long long key = ~0ull;
+        if constexpr (FMT == kInt8) {
+          // one copy of the 32-element body (instruction fetch, see int8_sse_row)
+#pragma unroll 1
+          for (int k = 0; k < CPI; ++k) {
+            const int c = c0 + k <= ch ? c0 + k : ch;
+            const float E = int8_sse_row<BS>(ar, ctab.val[c], __uint_as_float(ctab.cn[c].x), rows + bb * BS);
+            const unsigned long long kk = ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)(c + 1);
+            key = kk < key ? kk : key;
+          }
+        } else {
 #pragma unroll
-        for (int k = 0; k < CPI; ++k) {
-          const int c = c0 + k <= ch ? c0 + k : ch;
-          const float E = cand_sse<BS, MODE, DT, FMT>(ar, ctab, c);
-          // low word c + 1: 0 stays the naive scale, which wins ties
-          const unsigned long long kk = ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)(c + 1);
-          key = kk < key ? kk : key;
+          for (int k = 0; k < CPI; ++k) {
+            const int c = c0 + k <= ch ? c0 + k : ch;
+            const float E = cand_sse<BS, MODE, DT, FMT>(ar, ctab, c);
+            // low word c + 1: 0 stays the naive scale, which wins ties
+            const unsigned long long kk = ((unsigned long long)__float_as_uint(E) << 32) | (unsigned)(c + 1);
+            key = kk < key ? kk : key;
+          }
         }
         atomicMin(best + bb, key);
       }
