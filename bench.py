@@ -258,6 +258,11 @@ def _ev_time(fn, stream, reps=1):
     return e0.elapsed_time(e1) / reps
 
 
+def _all_ranks_ok(ok, ws, device):
+    """True on every rank when ok is true on every rank (one all-reduce)."""
+    return _max_over_ranks(0.0 if ok else 1.0, ws, device) == 0.0
+
+
 def _graph_time(fn, stream, reps, ws, device):
     """Device time of fn per call (max over ranks), replayed from a CUDA graph
     captured once, so no host gap between the call's launches falls inside
@@ -275,7 +280,7 @@ def _graph_time(fn, stream, reps, ws, device):
     except Exception as ex:  # noqa: BLE001
         g, err = None, type(ex).__name__
         torch.cuda.synchronize()
-    if _max_over_ranks(0.0 if g is not None else 1.0, ws, device) > 0:
+    if not _all_ranks_ok(g is not None, ws, device):
         how = "eager launches (graph capture failed" + (f": {err})" if err else " on another rank)")
         return _max_over_ranks(_ev_time(fn, stream, reps), ws, device), how
     g.replay()

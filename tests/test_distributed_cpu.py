@@ -187,3 +187,28 @@ def test_rank_that_never_arrives_is_an_error(tmp_path):
         assert not p.is_alive()
     err = (tmp_path / "fault.txt").read_text()
     assert err != "", "rank 0 should have seen an error"
+
+
+def _agree_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "bench_under_test", os.path.join(os.path.dirname(os.path.dirname(__file__)), "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    dev = torch.device("cpu")
+    res = {"all_ok": bench._all_ranks_ok(True, world, dev),
+           "one_failed": bench._all_ranks_ok(rank != 1, world, dev)}
+    torch.save(res, os.path.join(out_dir, f"a{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_graph_capture_agreement(tmp_path):
+    """bench.py times a pipeline with collectives from a CUDA graph only when
+    every rank captured it: one rank's failure must put all ranks on eager
+    launches, or their collectives would fall out of step."""
+    mp.spawn(_agree_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        res = torch.load(tmp_path / f"a{r}.pt")
+        assert res == {"all_ok": True, "one_failed": False}, (r, res)
