@@ -185,7 +185,17 @@ def quantize_many(weights, fmt, method, block_size=16, packed=True, return_dequa
         N = x.shape[0]
         bshape = (*W.shape[:-1], W.shape[-1] // block_size)
         if outputs is not None:
-            out = outputs[i]
+            out = tuple(outputs[i])
+            # the kernel writes through these pointers: layout, dtype and device must match exactly
+            want = ([(bshape, torch.uint8), ((*bshape, block_size // 2), torch.uint8),
+                     ((*bshape, block_size), torch.bfloat16)] if packed else
+                    [(bshape, torch.float32), ((*bshape, block_size), torch.float32),
+                     ((*bshape, block_size), torch.float32)])
+            assert len(out) == (3 if return_dequant else 2), f"outputs[{i}]: {len(out)} tensors"
+            for t, (shape, dtype) in zip(out, want):
+                assert (tuple(t.shape) == tuple(shape) and t.dtype == dtype and t.device == dev
+                        and t.is_contiguous()), (f"outputs[{i}]: expected a contiguous {dtype} tensor of shape "
+                                                 f"{tuple(shape)} on {dev}, got {t.dtype} {tuple(t.shape)} on {t.device}")
         elif packed:
             out = (torch.empty(bshape, dtype=torch.uint8, device=dev),
                    torch.empty(*bshape, block_size // 2, dtype=torch.uint8, device=dev))

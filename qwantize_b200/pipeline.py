@@ -49,6 +49,8 @@ class HostBatchQuantizer:
     def run_items(self, items, outputs: Optional[List[tuple]] = None, return_dequant: bool = True):
         """Like run(), with a (weight, fmt, method, block_size) spec per item."""
         lib = L.load()
+        if return_dequant and self.slots[0]["dq"] is None:
+            raise ValueError("return_dequant=True needs a HostBatchQuantizer built with with_dequant=True")
         res = []
         for i, (w, fmt, method, block_size) in enumerate(items):
             assert block_size in (16, 32)
@@ -69,7 +71,7 @@ class HostBatchQuantizer:
                     st.wait_event(slot["done"])  # the previous item of this slot is done
                 x = slot["x"][:n]
                 x.copy_(w.reshape(-1), non_blocking=True)
-                dq = slot["dq"][:n] if (return_dequant and slot["dq"] is not None) else None
+                dq = slot["dq"][:n] if return_dequant else None
                 L.check(lib.qz_quantize(
                     L.ptr(x), L.DTYPE_BF16, n // block_size, block_size, _FMT[fmt], _METHOD[method],
                     None, 0, None, None, None, L.ptr(slot["codes"]), L.ptr(slot["packed"]), L.ptr(dq),

@@ -66,3 +66,22 @@ def test_grouped_rejects_bad_arguments():
         _lib.QZ_ERR_INVALID
     assert L.qz_quantize_grouped(ctypes.c_void_p(0), 0, _lib.DTYPE_BF16, 16, _lib.FMT_NVFP4, _lib.METHOD_SSE,
                                  None) == _lib.QZ_OK
+
+
+def test_grouped_preallocated_outputs():
+    """outputs=: results written into the caller's tensors equal a fresh call;
+    a tensor of the wrong shape or dtype is refused before any launch."""
+    import qwantize_b200 as q
+    ws = _weights([(37, 544), (5, 96)], 23)
+    ref = q.quantize_many(ws, "nvfp4", "optimal", 16, packed=True, return_dequant=True)
+    outs = [tuple(torch.full_like(t, 7) for t in r) for r in ref]
+    got = q.quantize_many(ws, "nvfp4", "optimal", 16, packed=True, return_dequant=True, outputs=outs)
+    for r, g, o in zip(ref, got, outs):
+        for a, b, c in zip(r, g, o):
+            assert torch.equal(a.view(torch.uint8), b.view(torch.uint8)) and b.data_ptr() == c.data_ptr()
+    bad = [outs[0], (outs[1][0], outs[1][1][:, :-1], outs[1][2])]
+    with pytest.raises(AssertionError):
+        q.quantize_many(ws, "nvfp4", "optimal", 16, packed=True, return_dequant=True, outputs=bad)
+    bad = [outs[0], (outs[1][0], outs[1][1], outs[1][2].float())]
+    with pytest.raises(AssertionError):
+        q.quantize_many(ws, "nvfp4", "optimal", 16, packed=True, return_dequant=True, outputs=bad)

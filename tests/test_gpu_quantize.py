@@ -275,3 +275,9 @@ def test_host_pipeline_matches_device_path():
         assert torch.equal(codes, c2.cpu().reshape(-1))
         assert torch.equal(packed, p2.cpu().reshape(-1))
         assert torch.equal(dq.view(torch.int16), d2.cpu().reshape(-1).view(torch.int16))
+    # without device dequant buffers: codes only, and a dequant request is refused
+    hq2 = HostBatchQuantizer(256 * 1024, slots=2, with_dequant=False)
+    codes, packed = hq2.run([ws[0]], "nvfp4", "optimal", 16, return_dequant=False)[0]
+    assert torch.equal(codes, res[0][0]) and torch.equal(packed, res[0][1])
+    with pytest.raises(ValueError):
+        hq2.run([ws[0]], "nvfp4", "optimal", 16, return_dequant=True)
