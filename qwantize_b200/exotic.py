@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib as L
-from .core import _blocks, cuda_device, to_host_like
+from .core import _blocks, to_host_like
 
 _METHOD = {"naive": L.METHOD_NAIVE, "optimal": L.METHOD_SSE, "hoptimal": L.METHOD_HESSIAN}
 
